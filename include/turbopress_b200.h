@@ -1,0 +1,191 @@
+/*
+ * turbopress_b200 -- C ABI of the B200 (sm_100a) packed-TCQ decode path.
+ *
+ * The library replaces the GPU side of TurboPress's packed runtime
+ * (turbopress/runtime.py + turbopress/triton_kernel.py in
+ * godsonj64/turbopress v0.5.2).  Host code in any language binds these
+ * entry points with plain pointers and sizes; nothing here mentions torch.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are DEVICE pointers unless stated otherwise.  Buffers are
+ *     owned and allocated by the caller; no entry point allocates device
+ *     memory, synchronizes the device or the stream, or keeps a pointer
+ *     after it returns.  Every launch is enqueued on `stream` (a
+ *     cudaStream_t passed as void*, NULL = legacy default stream), so all
+ *     calls can be captured into a CUDA graph.
+ *   - Half-precision values travel as uint16_t bit patterns (IEEE fp16).
+ *   - n = out_features, d = in_features, bits = payload bits per weight,
+ *     n_states = trellis states S in {4, 8, 16, 64}.
+ *   - A status code is returned; on failure tp_last_error() describes it.
+ *     No entry point throws across the ABI.
+ *   - Thread safety: every entry point is reentrant; the only global state
+ *     is a per-thread error string and one-time per-device kernel attribute
+ *     setup.
+ */
+#ifndef TURBOPRESS_B200_H
+#define TURBOPRESS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TP_API __attribute__((visibility("default")))
+#else
+#define TP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int tp_status;
+#define TP_OK 0
+#define TP_ERR_ARG 1          /* bad argument (null pointer, bad size)          */
+#define TP_ERR_UNSUPPORTED 2  /* unsupported bits / n_states / block / batch    */
+#define TP_ERR_ALIGN 3        /* pointer or stride alignment requirement broken */
+#define TP_ERR_CUDA 4         /* a CUDA launch or runtime call failed           */
+#define TP_ERR_WORKSPACE 6    /* workspace missing or smaller than required     */
+
+/* Activation / output element types. */
+#define TP_F16 0
+#define TP_F32 1
+#define TP_BF16 2
+
+/* Version of this ABI (bumped on any signature change). */
+TP_API int tp_abi_version(void);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+TP_API const char* tp_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Format-v2 bit streams (little-endian within a byte, rows byte-aligned).
+ * ---------------------------------------------------------------------- */
+
+/* out[n, ceil(d*width/8)] = pack of vals[n, d] (uint8 values < 2^width).
+ * Replaces turbopress/runtime.py:73-90 (pack_le). */
+TP_API tp_status tp_pack_le(const uint8_t* vals, uint8_t* out, int64_t n, int64_t d,
+                     int width, void* stream);
+
+/* out[n, d] = unpack of packed[n, ceil(d*width/8)].
+ * Replaces turbopress/runtime.py:93-100 (unpack_le). */
+TP_API tp_status tp_unpack_le(const uint8_t* packed, uint8_t* out, int64_t n, int64_t d,
+                       int width, void* stream);
+
+/* levels[n, d] = member*4 + subset(window of path bits), zero-padded start.
+ * path_bits / member_codes are unpacked uint8 [n, d]; member may be NULL.
+ * Replaces turbopress/runtime.py:122-139 (window_decode_levels). */
+TP_API tp_status tp_window_decode_levels(const uint8_t* path_bits, const uint8_t* member_codes,
+                                  uint8_t* levels, int64_t n, int64_t d, int n_states,
+                                  void* stream);
+
+/* out[r1-r0, d] (fp16) = fp16(codebook[level] * scale[row]) for rows [r0, r1)
+ * of the format-v2 streams, bit-exact with the reference decode.
+ * path_packed: [n, ceil(d/8)], member_packed: [n, ceil(d*(bits-1)/8)] or NULL
+ * when bits == 1.  bits in [1, 7].
+ * Replaces turbopress/runtime.py:291-301 (PackedTCQLinear.decode_rows). */
+TP_API tp_status tp_decode_rows(const uint8_t* path_packed, const uint8_t* member_packed,
+                         const uint16_t* scales, const uint16_t* codebook, uint16_t* out,
+                         int64_t r0, int64_t r1, int64_t d, int bits, int n_states,
+                         void* stream);
+
+/* rot_scale[d] (fp16) = fp16((2*sign - 1) * inv_equil), signs_packed [1, ceil(d/8)].
+ * Replaces turbopress/runtime.py:245-249. */
+TP_API tp_status tp_rot_scale(const uint8_t* signs_packed, const uint16_t* inv_equil,
+                       uint16_t* rot_scale, int64_t d, void* stream);
+
+/* Format-v1 flat stream (numpy packbits, MSB-first, of LSB-first `width`-bit
+ * values over the whole [n, d] matrix, turbopress/pipeline.py:106-117) ->
+ * format-v2 row-aligned LE stream out[n, ceil(d*width/8)].
+ * Replaces the numpy unpack + pack_le of turbopress/runtime.py:428-447. */
+TP_API tp_status tp_v1_to_v2(const uint8_t* v1, uint8_t* out, int64_t n, int64_t d, int width,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
+ * Seeded randomized Hadamard rotation of activations.
+ * ---------------------------------------------------------------------- */
+
+/* z[B, d] = blockFWHT(x[B, d] * rot_scale[d]) over blocks of `block` columns
+ * (orthonormal Sylvester order), computed in fp32.  x_dtype / z_dtype are
+ * TP_F16, TP_F32 or TP_BF16; rows are contiguous (row stride d).
+ * block must be a power of two dividing d, 1 <= block <= 32768.
+ * Replaces turbopress/triton_kernel.py:235-260 (fwht_scale) and the torch
+ * path turbopress/runtime.py:192-208 + :322-323. */
+TP_API tp_status tp_rotate(const void* x, int x_dtype, const uint16_t* rot_scale, void* z,
+                    int z_dtype, int64_t B, int64_t d, int64_t block, void* stream);
+
+/* Load-time fold used by the "cached" mode (turbopress/runtime.py:278-286):
+ * w_out[n, d] (fp16) = fp16(blockFWHT(w_rot[n, d]) * post_scale[d]), with
+ * w_rot fp16 and post_scale = (2*sign-1) * inv_equil (the rot_scale vector). */
+TP_API tp_status tp_fold_rows(const uint16_t* w_rot, const uint16_t* post_scale, uint16_t* w_out,
+                       int64_t n, int64_t d, int64_t block, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Native true-rate tile layout ("TCQ stream") and the fused GEMV.
+ *
+ * The stream keeps exactly `bits` bits per weight (plus padding of n to a
+ * multiple of 16 rows and d to a multiple of 256 columns), re-arranged so a
+ * warp reads 16-row x 256-column tiles with coalesced 16-byte loads and
+ * decodes them with register bit-slicing.  It is derived data: built on the
+ * device from the format-v2 (or v1) streams at load time.
+ * ---------------------------------------------------------------------- */
+
+/* Bytes of the native stream for an [n, d] matrix at `bits` (1..4). */
+TP_API int64_t tp_stream_bytes(int64_t n, int64_t d, int bits);
+
+/* Build the native stream from format-v2 streams (layout of tp_decode_rows).
+ * stream_out must hold tp_stream_bytes(n, d, bits) bytes, 16-byte aligned.
+ * Replaces the load-time re-pack of turbopress/runtime.py:253-277. */
+TP_API tp_status tp_relayout_v2(const uint8_t* path_packed, const uint8_t* member_packed,
+                         uint8_t* stream_out, int64_t n, int64_t d, int bits,
+                         void* stream);
+
+/* Build the native stream straight from a format-v1 artifact matrix
+ * (flat MSB-first numpy packbits streams, turbopress/pipeline.py:106-117,
+ * :445-455).  path_bits: ceil(n*d/8) bytes; member_bits: ceil(n*d*(bits-1)/8)
+ * bytes or NULL when bits == 1.
+ * Replaces turbopress/runtime.py:417-452 (v1_payload_to_packed) + :253-277. */
+TP_API tp_status tp_relayout_v1(const uint8_t* path_bits, const uint8_t* member_bits,
+                         uint8_t* stream_out, int64_t n, int64_t d, int bits,
+                         void* stream);
+
+/* Bit-exact fp16 decode of rows [r0, r1) from the native stream (same values
+ * as tp_decode_rows on the source streams). */
+TP_API tp_status tp_decode_stream(const uint8_t* tcq_stream, const uint16_t* scales,
+                           const uint16_t* codebook, uint16_t* out, int64_t r0, int64_t r1,
+                           int64_t n, int64_t d, int bits, int n_states, void* stream);
+
+/* Device workspace (bytes) that tp_tcq_gemv needs for a given problem.
+ * The workspace must be zero-filled once when allocated; every call leaves
+ * its counters at zero again, so the same buffer serves any later call of
+ * equal or smaller size.  Calls that share a workspace must not overlap on
+ * the GPU (use one workspace per stream). */
+TP_API int64_t tp_gemv_workspace_bytes(int64_t B, int64_t n, int64_t d, int bits);
+
+/* y[B, n] = blockFWHT(x[B, d] * rot_scale) @ W'^T (+ bias), W' the dequantized
+ * rotated weights held in the native stream: the fused decode-in-GEMV.
+ * x_dtype / y_dtype in {TP_F16, TP_F32, TP_BF16}; bias fp16 [n] or NULL.
+ * bits in 1..4, n_states in {4, 8, 16, 64}, 1 <= B (batches above 32 run in
+ * chunks of 32).  Accumulates in fp32.  Deterministic (fixed reduction order).
+ * Replaces turbopress/triton_kernel.py:132-157 (packed_gemv) together with
+ * fwht_scale, i.e. PackedTCQLinear.forward in mode "triton"
+ * (turbopress/runtime.py:312-316, :332-334). */
+TP_API tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot_scale,
+                      const uint8_t* tcq_stream, const uint16_t* scales,
+                      const uint16_t* codebook, const uint16_t* bias, void* y, int y_dtype,
+                      int64_t B, int64_t n, int64_t d, int64_t block, int bits, int n_states,
+                      void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Reference-order GEMV straight from the format-v2 streams, any bits in 1..7:
+ * y[B, n] = z[B, d] @ decode_rows^T (+ bias), z fp32 rotated activations.
+ * Used for payloads the native stream does not cover (bits 5..7) and as an
+ * independent GPU cross-check.  Replaces the "tiled" forward loop of
+ * turbopress/runtime.py:324-331. */
+TP_API tp_status tp_gemv_v2(const float* z, const uint8_t* path_packed, const uint8_t* member_packed,
+                     const uint16_t* scales, const uint16_t* codebook, const uint16_t* bias,
+                     void* y, int y_dtype, int64_t B, int64_t n, int64_t d, int bits,
+                     int n_states, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURBOPRESS_B200_H */
