@@ -38,11 +38,32 @@ inline tp_status check_launch(const char* what) {
   return clear_ok();
 }
 
+// On failure the error is also cleared from the runtime's last-error slot so
+// it cannot be misattributed to a later launch check.
 #define TP_CUDA_TRY(call, what)                                                    \
   do {                                                                             \
     cudaError_t _e = (call);                                                       \
-    if (_e != cudaSuccess) return fail(TP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(_e)); \
+    if (_e != cudaSuccess) {                                                       \
+      (void)cudaGetLastError();                                                    \
+      return fail(TP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(_e));            \
+    }                                                                              \
   } while (0)
+
+// Raise a kernel's dynamic shared memory limit to at least `bytes` (once per
+// device and size).  `slot` is a per-kernel array of the sizes already set.
+template <class K>
+inline tp_status ensure_smem(K kernel, size_t bytes, int* slot, const char* what) {
+  int dev = 0;
+  TP_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (bytes <= 48 * 1024 || (size_t)__atomic_load_n(&slot[dev], __ATOMIC_ACQUIRE) >= bytes) return TP_OK;
+  TP_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes), what);
+  int cur = __atomic_load_n(&slot[dev], __ATOMIC_ACQUIRE);
+  while (cur < (int)bytes && !__atomic_compare_exchange_n(&slot[dev], &cur, (int)bytes, false, __ATOMIC_ACQ_REL,
+                                                          __ATOMIC_ACQUIRE)) {
+  }
+  return TP_OK;
+}
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -419,18 +419,8 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int sms) {
 template <int BITS, int S, int NT>
 tp_status launch_gemv_t(const GemvParams& p, const Plan& pl, cudaStream_t stream) {
   auto kern = tcq_gemv_kernel<BITS, S, NT>;
-  static std::mutex mu;
-  static bool done[64] = {false};
-  int dev = 0;
-  TP_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 64 && !done[dev]) {
-      TP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
-                  "cudaFuncSetAttribute(gemv)");
-      done[dev] = true;
-    }
-  }
+  static int smem_set[64] = {0};
+  if (tp_status s = ensure_smem(kern, pl.smem, smem_set, "cudaFuncSetAttribute(gemv)")) return s;
   dim3 grid(static_cast<unsigned>(pl.row_blocks), static_cast<unsigned>(pl.ksplit));
   kern<<<grid, Cfg<BITS>::kWarps * 32, pl.smem, stream>>>(p);
   return check_launch("tcq_gemv_kernel");

@@ -6,8 +6,6 @@
 // __syncthreads per group).  The Walsh-Hadamard stages commute, so the
 // grouping order is free; the orthonormal 1/sqrt(block) factor is applied
 // once on the way out (turbopress/runtime.py:192-208).
-#include <mutex>
-
 #include "tp_rotate.cuh"
 
 using namespace tp;
@@ -89,11 +87,6 @@ __global__ void rotate_kernel(RotateArgs a) {
   }
 }
 
-namespace {
-std::mutex g_attr_mu;
-bool g_attr_done[64] = {false};
-}  // namespace
-
 tp_status launch_rotate(RotateArgs a, int64_t rows, cudaStream_t stream) {
   if (a.block < 1 || (a.block & (a.block - 1)) || a.d % a.block)
     return fail(TP_ERR_ARG, "block must be a power of two dividing d (d=%lld, block=%lld)", (long long)a.d,
@@ -111,17 +104,8 @@ tp_status launch_rotate(RotateArgs a, int64_t rows, cudaStream_t stream) {
   a.per = static_cast<int>(per);
   const int64_t count = per * a.block;
   const size_t smem = static_cast<size_t>(count) * sizeof(float);
-  int dev = 0;
-  TP_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  {
-    std::lock_guard<std::mutex> lk(g_attr_mu);
-    if (dev < 64 && !g_attr_done[dev]) {
-      TP_CUDA_TRY(cudaFuncSetAttribute(rotate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kMaxRotateBlock * (int)sizeof(float)),
-                  "cudaFuncSetAttribute(rotate)");
-      g_attr_done[dev] = true;
-    }
-  }
+  static int smem_set[64] = {0};
+  if (tp_status s = ensure_smem(rotate_kernel, smem, smem_set, "cudaFuncSetAttribute(rotate)")) return s;
   int threads = static_cast<int>(count / 8);
   if (threads < 32) threads = 32;
   if (threads > 1024) threads = 1024;
