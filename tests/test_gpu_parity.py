@@ -203,7 +203,12 @@ def test_gemv_dtypes_and_shapes(dtype):
     y = m(x)
     assert y.dtype == dtype and y.shape == (2, 3, 96)
     ref = O.forward_fp32(p, x.float().cpu().numpy())
-    assert rel_l2(y.float().cpu().numpy(), ref) < REL_L2_TOL
+    # a bf16 output alone carries ~2^-9 relative rounding; the fp32 result of
+    # the same kernel must meet the 1e-3 bound
+    tol = 4e-3 if dtype == torch.bfloat16 else REL_L2_TOL
+    assert rel_l2(y.float().cpu().numpy(), ref) < tol
+    y32 = m(x.float())
+    assert rel_l2(y32.cpu().numpy(), ref) < REL_L2_TOL
 
 
 @pytest.mark.parametrize("bits", [5, 6, 7])
@@ -236,6 +241,20 @@ def test_gemv_deterministic_and_graph_capturable():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(yg, y1)
+
+
+def test_shared_workspace_across_shapes():
+    # calls of different row-block counts share the per-device workspace
+    from turbopress_b200 import PackedTCQLinear
+    big = O.random_payload(9728, 512, 3, 64, seed=1)
+    small = O.random_payload(512, 4096, 3, 64, seed=2)
+    mb, ms = PackedTCQLinear(to_dev(big), mode="cuda"), PackedTCQLinear(to_dev(small), mode="cuda")
+    xb = np.random.default_rng(0).standard_normal((1, 512)).astype(np.float16)
+    xs = np.random.default_rng(1).standard_normal((1, 4096)).astype(np.float16)
+    rb, rs = O.forward_fp32(big, xb), O.forward_fp32(small, xs)
+    for _ in range(3):
+        assert rel_l2(mb(torch.from_numpy(xb).to(DEV)).float().cpu().numpy(), rb) < REL_L2_TOL
+        assert rel_l2(ms(torch.from_numpy(xs).to(DEV)).float().cpu().numpy(), rs) < REL_L2_TOL
 
 
 # ---------------------------------------------------------------------------

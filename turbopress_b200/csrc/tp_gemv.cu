@@ -35,6 +35,11 @@ using namespace tp;
 namespace {
 
 constexpr int kMaxBatchPerLaunch = 32;  // 4 n-tiles of the m16n8k16 MMA
+// The workspace starts with a fixed-size block of split-K counters, so calls
+// of different shapes sharing one workspace never overlap each other's
+// counters with their activation or partial-sum regions.
+constexpr int64_t kMaxRowBlocks = 16384;
+constexpr int64_t kCounterBytes = kMaxRowBlocks * 4;
 
 template <int BITS>
 struct Cfg {
@@ -409,7 +414,7 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int sms) {
   const int64_t slice_units = (pl.units_k + pl.ksplit - 1) / pl.ksplit;
   const int lut = bits == 4 ? Cfg<4>::kLutBytes : Cfg<3>::kLutBytes;
   pl.smem = static_cast<size_t>(lut + (Bc * slice_units * 32 + 4) * 16);
-  pl.ws_counters = align256(pl.row_blocks * 4);
+  pl.ws_counters = kCounterBytes;
   pl.ws_z = align256(Bc * d_pad * 2);
   pl.ws_partial = pl.ksplit > 1 ? align256((int64_t)pl.ksplit * Bc * n_pad * 4) : 0;
   pl.ws_total = pl.ws_counters + pl.ws_z + pl.ws_partial;
@@ -519,6 +524,8 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
   if (B == 0 || n == 0) return clear_ok();
   if (d == 0) return fail(TP_ERR_ARG, "tp_tcq_gemv: d must be positive");
   const Plan pl = make_plan(B, n, d, bits, sm_count());
+  if (pl.row_blocks > kMaxRowBlocks)
+    return fail(TP_ERR_UNSUPPORTED, "tp_tcq_gemv: n=%lld exceeds the supported maximum row count", (long long)n);
   if (!workspace || workspace_bytes < pl.ws_total)
     return fail(TP_ERR_WORKSPACE, "tp_tcq_gemv: workspace of %lld bytes required (got %lld)", (long long)pl.ws_total,
                 (long long)workspace_bytes);
