@@ -174,6 +174,23 @@ TP_API tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot_sca
                       int64_t B, int64_t n, int64_t d, int64_t block, int bits, int n_states,
                       void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free form of tp_tcq_gemv, for callers that cannot allocate
+ * device memory (e.g. plugins whose host engine owns all allocations, or
+ * loops where a cudaMalloc is not allowed).  No counterpart in the
+ * reference.  Same arguments and result as tp_tcq_gemv without the
+ * workspace: the scratch lives in an 8 MiB array inside this library,
+ * held on every GPU that loads it until the process exits.  Problems whose
+ * tp_gemv_workspace_bytes() exceed 8 MiB are rejected with
+ * TP_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address and clears its counters; make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (concurrent streams) race and must be serialized by the caller. */
+TP_API tp_status tp_tcq_gemv_noalloc(const void* x, int x_dtype, const uint16_t* rot_scale,
+                                     const uint8_t* tcq_stream, const uint16_t* scales,
+                                     const uint16_t* codebook, const uint16_t* bias, void* y,
+                                     int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block,
+                                     int bits, int n_states, void* stream);
+
 /* Reference-order GEMV straight from the format-v2 streams, any bits in 1..7:
  * y[B, n] = z[B, d] @ decode_rows^T (+ bias), z fp32 rotated activations.
  * Used for payloads the native stream does not cover (bits 5..7) and as an
