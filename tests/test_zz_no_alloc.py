@@ -55,8 +55,10 @@ def test_noalloc_rejects_oversized_problems():
         pytest.skip("needs a CUDA device")
     from turbopress_b200 import _abi
     L = _abi.lib()
-    # 32 rows of a 28672x28672 layer need far more than the built-in scratch
-    assert L.tp_gemv_workspace_bytes(32, 28672, 28672, 2) > (8 << 20)
-    st = L.tp_tcq_gemv_noalloc(1, 0, 1, 16, 1, 1, None, 1, 0, 32, 28672, 28672, 4096, 2, 64, None)
+    # 32 rows of a layer with d = 262144 need > 8 MiB of scratch; null data
+    # pointers make sure nothing could launch even if the size guard failed
+    assert L.tp_gemv_workspace_bytes(32, 4096, 262144, 2) > (8 << 20)
+    st = L.tp_tcq_gemv_noalloc(None, 0, None, None, None, None, None, None, 0, 32, 4096, 262144, 65536, 2, 64,
+                               None)
     assert st == _abi.TP_ERR_UNSUPPORTED
     assert b"built-in maximum" in L.tp_last_error()

@@ -160,10 +160,9 @@ __host__ __device__ inline int64_t stream_bytes(int64_t n, int64_t d, int bits) 
 }
 
 // column (0..7 inside an 8-column group) -> (word w, half h) of the pair byte
+// r: 0->a.lo 4->a.hi 2->b.lo 6->b.hi 1->c.lo 5->c.hi 3->d.lo 7->d.hi
 __host__ __device__ inline void col_slot(int r, int& w, int& h) {
-  // r: 0->a.lo 4->a.hi 2->b.lo 6->b.hi 1->c.lo 5->c.hi 3->d.lo 7->d.hi
-  const int wtab[8] = {0, 2, 1, 3, 0, 2, 1, 3};
-  w = wtab[r];
+  w = ((r & 1) << 1) | ((r >> 1) & 1);
   h = r >> 2;
 }
 

@@ -1,40 +1,55 @@
-// Fused packed-TCQ GEMV / skinny GEMM for batch 1..32 on sm_100a.
+// Fused rotate + packed-TCQ GEMV / skinny GEMM for batch 1..32 on sm_100a.
 //
-// y[b, r] = scale[r] * sum_c codebook[level(r, c)] * z[b, c]  (+ bias[r])
+// y[b, r] = scale[r] * sum_c codebook[level(r, c)] * z[b, c]  (+ bias[r]),
+// z = blockFWHT(x * rot_scale) computed inside the kernel.
 //
-// Data path per warp (16 output rows, see tp_common.cuh for the stream
-// layout):
-//   1. coalesced 16-byte non-allocating loads of the true-rate stream
-//      (bits words per row per 32 columns), prefetched one unit ahead;
-//   2. the 6-bit trellis halo of every 32-column chunk comes from the
-//      neighbouring lane by one warp shuffle;
-//   3. register bit-slicing: the two subset bit-planes are GF(2)
-//      convolutions of the path word (funnel shifts + XOR), merged with the
-//      member bits into four "level words" of 8 nibbles (LOP3 selects);
-//   4. each byte of a level word (two 4-bit levels) is turned into a shared
-//      memory address by ONE byte permute (byte | lane*4) and looked up in a
-//      lane-replicated pair table holding half2(codebook[lo], codebook[hi]),
-//      so 32 lanes hit 32 distinct banks;
-//   5. the half2 weight pairs are the A fragments of a warp-level
-//      m16n8k16 tensor-core MMA (fp32 accumulate) against the rotated
-//      activations held in shared memory (B fragments), so the reduction
-//      over columns costs one MMA per 256 weights instead of 128 HFMA2;
-//   6. split-K over CTAs, reduced deterministically by the last CTA of each
-//      row block (counter in the workspace), scale/bias/cast fused.
+// One launch per linear.  CTA = 8 warps = RT row tiles (16 rows each) x KW
+// warps along K; a cluster of `ksplit` CTAs shares each row block's K range.
+// Per CTA:
+//   1. programmatic dependent launch: start weight loads (independent of the
+//      previous kernel) and build the pair table, then griddepcontrol.wait;
+//   2. rotate the CTA's K-slice of x (fp32 block FWHT in shared memory) into
+//      fp16 activations in the decoder's permuted pair order;
+//   3. per warp: coalesced 16-byte non-allocating loads of the true-rate
+//      stream (bits words per row per 32 columns), trellis halo by one warp
+//      shuffle, register bit-slicing (GF(2) convolution of the path word ->
+//      subset planes -> four "level words" of 8 nibbles), one byte permute
+//      per weight pair to address a lane-replicated pair table holding
+//      half2(codebook[lo], codebook[hi]) (32 lanes, 32 banks), and the pairs
+//      as A fragments of a warp-level m16n8k16 MMA with fp32 accumulation
+//      (one MMA per 256 weights);
+//   4. reduce KW warps in shared memory, then the cluster's CTAs through
+//      distributed shared memory (deterministic order), scale/bias/cast.
+//      Above 8 K-splits the partials go through the caller's workspace and
+//      the last CTA of a row block reduces them.
 //
 // 4-bit payloads (5-bit levels) use a 1024-entry pair table: the two fifth
-// level bits are carried in bit 7 and bit 16 of the address via a second
-// permute source (see build_lut / lut_addr4).
+// level bits ride in address bits 7 and 16 via a second permute source.
+#include <cooperative_groups.h>
+
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "tp_rotate.cuh"
 
+namespace cg = cooperative_groups;
 using namespace tp;
 
 namespace {
 
 constexpr int kMaxBatchPerLaunch = 32;  // 4 n-tiles of the m16n8k16 MMA
+constexpr int kWarps = 8;               // warps per CTA (RT * KW)
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxCluster = 8;          // portable cluster size
+constexpr int kMaxFusedBlock = 8192;    // Hadamard blocks rotated in-kernel
+constexpr int kScratchFloats = 8192;    // fp32 FWHT scratch (32 KB)
+constexpr int kMaxSlots = 16;           // weight units in flight per warp
+// dynamic shared memory per CTA (227 KB opt-in minus the static part)
+constexpr size_t kMaxDynSmem = 227u * 1024u - 2048u;
+// Bounded mbarrier wait: ~2^26 polls (seconds); the copies complete in
+// microseconds, so running out means the hardware misbehaved.
+constexpr unsigned kMaxPolls = 1u << 26;
 // The workspace starts with a fixed-size block of split-K counters, so calls
 // of different shapes sharing one workspace never overlap each other's
 // counters with their activation or partial-sum regions.
@@ -44,25 +59,33 @@ constexpr int64_t kCounterBytes = kMaxRowBlocks * 4;
 template <int BITS>
 struct Cfg {
   static constexpr int kLutBytes = BITS == 4 ? 131072 : 65536;
-  static constexpr int kWarps = BITS == 4 ? 16 : 8;
 };
+
 
 struct GemvParams {
   const uint4* stream;
   const uint16_t* scales;
   const uint16_t* bias;
   const uint16_t* codebook;
-  const uint4* zperm;  // [B][d_pad] fp16, permuted pair order
+  const void* x;             // [B][d] activations (x_dtype)
+  const uint16_t* rot_scale;
+  const uint4* zperm;        // pre-rotated [B][d_pad] fp16 (only when block > kMaxFusedBlock)
   void* y;
-  float* partial;      // [ksplit][B][n_pad]
-  unsigned* counters;  // [row_blocks]
-  int y_dtype;
+  float* partial;            // [ksplit][B][n_pad] (global split-K only)
+  unsigned* counters;        // [row_blocks]      (global split-K only)
+  int x_dtype, y_dtype;
   int B;
-  int64_t n;
-  int64_t n_pad;
-  int64_t d_pad;
+  int64_t n, n_pad, d, d_pad;
   int units_k;
-  int ksplit;
+  int block, lg_block;
+  float norm;
+  int rt;        // row tiles per CTA
+  int kw;        // warps along K per CTA (rt * kw == kWarps)
+  int ksplit;    // CTAs along K
+  int cluster;   // 1: reduce the ksplit CTAs through DSMEM
+  int zrows_per_pass;
+  int slots;     // weight units staged per warp (ring depth)
+  uint32_t w_off, z_off, scratch_off, red_off;  // shared-memory carve-up (bytes)
 };
 
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -88,27 +111,118 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// --- bulk-copy staging (TMA engine, no multicast) --------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// arrive + expect `bytes`, then copy global -> shared completing on `bar`
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+#if TP_CHECKED
+  {
+    extern __shared__ unsigned char smem[];
+    const uint32_t lo = smem_u32(smem), hi = lo + dyn_smem_size(), d = smem_u32(dst);
+    if ((d & 15u) || (reinterpret_cast<uintptr_t>(src) & 15u) || (bytes & 15u) || d < lo || d + bytes > hi) {
+      trace_bad(2, ((unsigned long long)d << 32) | bytes, ((unsigned long long)lo << 32) | hi);
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+      return;
+    }
+  }
+#endif
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// true when the phase with `parity` completed; false after kMaxPolls polls
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  const uint32_t a = smem_u32(bar);
+  for (unsigned i = 0; i < kMaxPolls; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+#ifdef TP_TRACE
+// Development-only phase timeline (built only with -DTP_TRACE, never in the
+// shipped library): thread 0 of each CTA stamps %globaltimer per phase.
+static __device__ unsigned long long g_trace[8192][16];
+__device__ __forceinline__ void trace(int k) {
+  if (threadIdx.x == 0) {
+    const unsigned cta = blockIdx.x * gridDim.y + blockIdx.y;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (cta < 8192) g_trace[cta][k] = t;
+  }
+}
+// record the first layout / bounds violation of a CTA in slots 12..15
+__device__ __forceinline__ void trace_bad(unsigned code, unsigned long long a, unsigned long long b) {
+  const unsigned cta = blockIdx.x * gridDim.y + blockIdx.y;
+  if (cta < 8192 && atomicCAS(&g_trace[cta][12], 0ull, (unsigned long long)code) == 0ull) {
+    g_trace[cta][13] = a;
+    g_trace[cta][14] = b;
+    g_trace[cta][15] = threadIdx.x;
+  }
+}
+__device__ __forceinline__ unsigned dyn_smem_size() {
+  unsigned v;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
+  return v;
+}
+#define TP_CHECKED 1
+#else
+__device__ __forceinline__ void trace(int) {}
+#define TP_CHECKED 0
+#endif
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Pair table.  bits <= 3: entry e (byte of a level word) at byte offset
-// e*256 + lane*4 holds half2(cb[lo(e)], cb[hi(e)]); levels ignore nibble bits
-// above the level width.  bits == 4: entry key k = m2lo<<7 | byte<<8 |
-// m2hi<<16 (word offset k + lane*4), levels (byte nibble | m2 << 4).
+// e*256 + lane*4 holds half2(cb[lo(e)], cb[hi(e)]); nibble bits above the
+// level width are ignored.  bits == 4: key k = m2lo<<7 | byte<<8 | m2hi<<16
+// (+ lane*4) holds half2(cb[byte&15 | m2lo<<4], cb[byte>>4 | m2hi<<4]).
+// The codebook (<= 32 fp16) sits one entry per lane and is read by shuffle;
+// each warp instruction stores four 128-byte table rows.
 template <int BITS>
-__device__ void build_lut(uint32_t* lut, const uint16_t* __restrict__ cb, int tid, int nthreads) {
-  const int lane = tid & 31;
-  const int warp = tid >> 5, nwarps = nthreads >> 5;
-  if (BITS <= 3) {
-    const unsigned lmask = (1u << (BITS + 1)) - 1u;
-    for (int e = warp; e < 256; e += nwarps) {
-      const uint32_t lo = cb[e & 15 & lmask], hi = cb[(e >> 4) & lmask];
-      lut[e * 64 + lane] = lo | (hi << 16);
+__device__ __forceinline__ void build_lut(unsigned char* lut, const uint16_t* __restrict__ cb, int warp, int lane) {
+  constexpr int kCb = 1 << (BITS + 1);
+  const uint32_t cbv = lane < kCb ? cb[lane] : 0u;
+  const int row = lane >> 3, col = lane & 7;
+  constexpr int kEntries = BITS <= 3 ? 256 : 1024;
+  for (int e0 = warp * 4; e0 < kEntries; e0 += kWarps * 4) {
+    const int e = e0 + row;
+    uint32_t lo, hi;
+    int off;
+    if (BITS <= 3) {
+      constexpr unsigned lmask = (1u << (BITS + 1)) - 1u;
+      lo = __shfl_sync(0xffffffffu, cbv, e & 15 & lmask);
+      hi = __shfl_sync(0xffffffffu, cbv, (e >> 4) & lmask);
+      off = e * 256;
+    } else {
+      const int byte = e & 255, m2lo = (e >> 8) & 1, m2hi = e >> 9;
+      lo = __shfl_sync(0xffffffffu, cbv, (byte & 15) | (m2lo << 4));
+      hi = __shfl_sync(0xffffffffu, cbv, (byte >> 4) | (m2hi << 4));
+      off = (m2lo << 7) | (byte << 8) | (m2hi << 16);
     }
-  } else {
-    for (int k = warp; k < 1024; k += nwarps) {
-      const int byte = k & 255, m2lo = (k >> 8) & 1, m2hi = k >> 9;
-      const uint32_t lo = cb[(byte & 15) | (m2lo << 4)], hi = cb[(byte >> 4) | (m2hi << 4)];
-      const int off = (m2lo << 7) | (byte << 8) | (m2hi << 16);
-      lut[(off >> 2) + lane] = lo | (hi << 16);
-    }
+    const uint32_t v = lo | (hi << 16);
+    *reinterpret_cast<uint4*>(lut + off + col * 16) = make_uint4(v, v, v, v);
   }
 }
 
@@ -164,10 +278,10 @@ __device__ __forceinline__ uint32_t x4(uint32_t M2, int w, int q, uint32_t lanep
 }
 
 template <int BITS, int S, int NT>
-__device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t lanew, const uint4* zq_base,
+__device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t lanew, const uint4* zq,
                                               uint32_t Pg, uint32_t Hg, uint32_t Pq, uint32_t Hq, uint32_t Mg0,
                                               uint32_t Mg1, uint32_t Mg2, uint32_t Mq0, uint32_t Mq1, uint32_t Mq2,
-                                              const int* zoff, float (*acc)[4]) {
+                                              const int* zoff, float (*acc)[NT][4]) {
   uint32_t Lg[4], Lq[4];
   {
     uint32_t A, Bm, Cw, Dm;
@@ -180,11 +294,12 @@ __device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t
   for (int w = 0; w < 4; ++w) {
     uint4 zv[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) zv[nt] = zq_base[zoff[nt] + w];
+    for (int nt = 0; nt < NT; ++nt) zv[nt] = zq[zoff[nt] + w];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       uint32_t a0, a1, a2, a3;
       if (BITS <= 3) {
+        // [lane*4, level byte, 0, 0] = byte*256 + lane*4
         const uint32_t s0 = 0x5504u | ((2u * q) << 4), s1 = 0x5504u | ((2u * q + 1u) << 4);
         a0 = lds32(lut, prmt(Lg[w], lanew, s0));
         a2 = lds32(lut, prmt(Lg[w], lanew, s1));
@@ -202,142 +317,313 @@ __device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t
       for (int nt = 0; nt < NT; ++nt) {
         const uint32_t b0 = q == 0 ? zv[nt].x : zv[nt].z;
         const uint32_t b1 = q == 0 ? zv[nt].y : zv[nt].w;
-        mma16816(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma16816(acc[q][nt], a0, a1, a2, a3, b0, b1);
       }
     }
   }
 }
 
+// Warp-local butterflies over index bits [0, lg) of s[0, 2^lg): radix-8
+// groups per lane, __syncwarp between groups (compact code; no CTA barrier).
+__device__ __forceinline__ void fwht_warp(float* s, int lg, int lane) {
+  for (int b0 = 0; b0 < lg; b0 += 3) {
+    const int nb = lg - b0 < 3 ? lg - b0 : 3;
+    const int G = 1 << nb;
+    const int groups = (1 << lg) >> nb;
+    for (int grp = lane; grp < groups; grp += 32) {
+      const int lo = grp & ((1 << b0) - 1);
+      const int base = ((grp >> b0) << (b0 + nb)) | lo;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < G) v[e] = s[base + (e << b0)];
+#pragma unroll
+      for (int h = 1; h < 8; h <<= 1) {
+        if (h >= G) break;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < G && !(e & h)) {
+            const float x0 = v[e], x1 = v[e + h];
+            v[e] = x0 + x1;
+            v[e + h] = x0 - x1;
+          }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < G) s[base + (e << b0)] = v[e];
+    }
+    __syncwarp();
+  }
+}
+
+// Rotated activations of the CTA's K-slice [c0, c0 + ncols) into zs
+// ([B][ncols] fp16, permuted pair order inside each 32-column chunk), with
+// columns >= d zeroed.  The covering Hadamard blocks of x * rot_scale are
+// staged in fp32 scratch (rows in passes of zrows_per_pass); blocks of up to
+// 1024 columns are transformed one per warp, larger ones by the whole CTA.
+__device__ void rotate_slice(const GemvParams& p, int64_t c0, int ncols, __half* zs, float* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t c1 = c0 + ncols;
+  const int64_t vend = c1 < p.d ? c1 : p.d;  // valid columns end
+  const int B = p.B;
+  if (p.zperm) {  // pre-rotated by a separate launch (very large Hadamard blocks)
+    const int q = ncols / 8;  // uint4 per row
+    for (int i = tid; i < B * q; i += kThreads) {
+      const int b = i / q, r = i - b * q;
+      reinterpret_cast<uint4*>(zs)[i] = p.zperm[(int64_t)b * (p.d_pad / 8) + c0 / 8 + r];
+    }
+    return;
+  }
+  if (vend < c1) {  // zero the slice columns past d
+    const int nz = static_cast<int>(c1 - (vend > c0 ? vend : c0));
+    for (int i = tid; i < B * nz; i += kThreads) {
+      const int b = i / nz;
+      const int lc = static_cast<int>(c1 - nz - c0) + (i - b * nz);
+      zs[b * ncols + (lc & ~31) + zperm_pos(lc & 31)] = __float2half_rn(0.f);
+    }
+  }
+  if (c0 >= p.d) return;
+  const int64_t blk = p.block;
+  const int64_t s0 = c0 / blk * blk;
+  const int64_t s1 = (vend + blk - 1) / blk * blk;
+  const int span = static_cast<int>(s1 - s0);
+  for (int b0 = 0; b0 < B; b0 += p.zrows_per_pass) {
+    const int rows = B - b0 < p.zrows_per_pass ? B - b0 : p.zrows_per_pass;
+    for (int i = tid; i < rows * span; i += kThreads) {
+      const int rr = i / span, c = i - rr * span;
+      const int64_t col = s0 + c;
+      scratch[i] = load_as_float(p.x, (int64_t)(b0 + rr) * p.d + col, p.x_dtype) * h2f_bits(p.rot_scale[col]);
+    }
+    __syncthreads();
+    trace(8);
+    if (blk <= 1024) {
+      const int nblocks = rows * span / static_cast<int>(blk);
+      for (int k = warp; k < nblocks; k += kWarps) fwht_warp(scratch + (size_t)k * blk, p.lg_block, lane);
+      __syncthreads();
+    } else {
+      fwht_shared(scratch, rows * span, p.lg_block);
+    }
+    trace(9);
+    for (int i = tid; i < rows * ncols; i += kThreads) {
+      const int rr = i / ncols, lc = i - rr * ncols;
+      const int64_t col = c0 + lc;
+      if (col < vend) zs[(b0 + rr) * ncols + (lc & ~31) + zperm_pos(lc & 31)] =
+          __float2half_rn(scratch[rr * span + (int)(col - s0)] * p.norm);
+    }
+    __syncthreads();
+  }
+}
+
 template <int BITS, int S, int NT>
-__global__ void __launch_bounds__(Cfg<BITS>::kWarps * 32) tcq_gemv_kernel(GemvParams p) {
-  constexpr int WARPS = Cfg<BITS>::kWarps;
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* lut = smem;
-  uint4* zs = reinterpret_cast<uint4*>(smem + Cfg<BITS>::kLutBytes);
+  __half* zs = reinterpret_cast<__half*>(smem + p.z_off);
+  float* scratch = reinterpret_cast<float*>(smem + p.scratch_off);
+  float* red = reinterpret_cast<float*>(smem + p.red_off);
   __shared__ unsigned s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
+  const int rtl = warp % p.rt, kwi = warp / p.rt;
   const int ks = blockIdx.y;
   const int u0 = static_cast<int>((int64_t)ks * p.units_k / p.ksplit);
   const int u1 = static_cast<int>((int64_t)(ks + 1) * p.units_k / p.ksplit);
-  const int nunits = u1 - u0;
-  const int64_t rt = (int64_t)blockIdx.x * WARPS + warp;
+  const int U = u1 - u0;
+  const int wu0 = u0 + kwi * U / p.kw, wu1 = u0 + (kwi + 1) * U / p.kw;
+  const int nunits = wu1 - wu0;
+  const int64_t rt = (int64_t)blockIdx.x * p.rt + rtl;
   const bool active = rt * kTileRows < p.n_pad;
 
-  // ---- prologue: first stream loads in flight before the table build ----
-  const uint4* wp = p.stream + ((rt * p.units_k + u0) * 32 + lane) * BITS;
-  const int64_t ustride = 32 * BITS;
-  uint4 cur[BITS];
-  uint32_t prevP1g = 0u, prevP1q = 0u;
-  if (active && nunits > 0) {
-#pragma unroll
-    for (int i = 0; i < BITS; ++i) cur[i] = ldg_stream(wp + i);
-    if (u0 > 0) {
-      const uint4 pv = ldg_stream(wp - ustride);
-      prevP1g = pv.z;
-      prevP1q = pv.w;
-    }
-  }
+  trace(0);
+  // the next kernel in the stream may start its own prologue now; it waits
+  // for this grid's completion before touching our outputs
+  pdl_trigger();
 
-  build_lut<BITS>(reinterpret_cast<uint32_t*>(lut), p.codebook, tid, WARPS * 32);
-  const int zchunk = nunits * 32;  // uint4 per batch row in the slice
-  for (int i = tid; i < p.B * zchunk; i += WARPS * 32) {
-    const int b = i / zchunk, r = i - b * zchunk;
-    zs[i] = p.zperm[(int64_t)b * (p.d_pad / 8) + (int64_t)u0 * 32 + r];
+  // ---- prologue independent of the previous kernel ----
+  // Each warp's weights (row tile rt, units [wu0, wu1)) are one contiguous
+  // run of the stream; lane 0 streams it unit by unit into the warp's ring
+  // of `slots` shared-memory units with bulk copies, all in flight now.
+  __shared__ __align__(8) uint64_t s_bar[kWarps][kMaxSlots];
+  __shared__ int s_fail;
+  constexpr unsigned kUnitBytes = 32u * 16u * BITS;
+  unsigned char* ring = smem + p.w_off + (size_t)warp * p.slots * kUnitBytes;
+  const unsigned char* wsrc =
+      reinterpret_cast<const unsigned char*>(p.stream) + ((size_t)(rt * p.units_k + wu0)) * kUnitBytes;
+  const bool staged = active && nunits > 0;
+  if (tid == 0) s_fail = 0;
+  if (staged && lane == 0) {
+    const int first = nunits < p.slots ? nunits : p.slots;
+    for (int s = 0; s < first; ++s) mbar_init(&s_bar[warp][s], 1);
+    fence_mbar_init();
+    for (int s = 0; s < first; ++s) bulk_load(ring + (size_t)s * kUnitBytes, wsrc + (size_t)s * kUnitBytes,
+                                              kUnitBytes, &s_bar[warp][s]);
   }
-  if (tid < 4) zs[p.B * zchunk + tid] = make_uint4(0, 0, 0, 0);
+  uint32_t prevP1g = 0u, prevP1q = 0u;  // trellis halo: last chunk before wu0
+  if (staged && wu0 > 0) {
+    const uint4 pv = ldg_stream(reinterpret_cast<const uint4*>(wsrc - kUnitBytes) + lane * BITS);
+    prevP1g = pv.z;
+    prevP1q = pv.w;
+  }
+  trace(1);
+  build_lut<BITS>(lut, p.codebook, warp, lane);
+  trace(2);
+
+  // ---- activations: wait for the producer of x, then rotate our slice ----
+  pdl_wait();
+  trace(3);
+  const int ncols = U * kUnitCols;
+  rotate_slice(p, (int64_t)u0 * kUnitCols, ncols, zs, scratch);
+  if (tid < 16) reinterpret_cast<uint32_t*>(zs + p.B * ncols)[tid] = 0u;  // zero block (64 B)
   __syncthreads();
+  trace(4);
 
-  float acc[NT][4];
+  // two independent accumulator chains (byte pairs q = 0 / 1) keep the
+  // dependent MMA sequence short
+  float acc[2][NT][4];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[q][nt][0] = acc[q][nt][1] = acc[q][nt][2] = acc[q][nt][3] = 0.f;
 
-  if (active) {
-    // per n-tile z pointers: batch row nt*8+g, or the zero block
+  if (staged) {
+    const uint4* zq = reinterpret_cast<const uint4*>(zs);
+    const int zchunk = ncols / 8;  // uint4 per batch row
     int zbase[NT], zunit[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int bn = nt * 8 + g;
-      zbase[nt] = bn < p.B ? bn * zchunk + t * 4 : p.B * zchunk;
+      zbase[nt] = bn < p.B ? bn * zchunk + (wu0 - u0) * 32 + t * 4 : p.B * zchunk;
       zunit[nt] = bn < p.B ? 1 : 0;
     }
     const uint32_t lanew = BITS <= 3 ? (uint32_t)lane * 4u : (uint32_t)lane * 4u * 0x10001u;
     const int src = (lane & ~3) | ((t + 3) & 3);
+    bool ok = true;
     for (int i = 0; i < nunits; ++i) {
-      uint4 nxt[BITS];
-      if (i + 1 < nunits) {
+      const int s = i % p.slots;
+      if (!mbar_wait(&s_bar[warp][s], (unsigned)(i / p.slots) & 1u)) {
+        ok = false;
+        break;
+      }
+      uint4 cur[BITS];
+      const uint4* su = reinterpret_cast<const uint4*>(ring + (size_t)s * kUnitBytes) + lane * BITS;
 #pragma unroll
-        for (int k = 0; k < BITS; ++k) nxt[k] = ldg_stream(wp + (i + 1) * ustride + k);
+      for (int k = 0; k < BITS; ++k) cur[k] = su[k];
+      __syncwarp();
+      if (lane == 0 && i + p.slots < nunits) {  // refill the slot just drained
+        fence_proxy_async();
+        bulk_load(ring + (size_t)s * kUnitBytes, wsrc + (size_t)(i + p.slots) * kUnitBytes, kUnitBytes,
+                  &s_bar[warp][s]);
       }
       const uint32_t P0g = cur[0].x, P0q = cur[0].y, P1g = cur[0].z, P1q = cur[0].w;
-      // halos: neighbour lane's chunk (t-1), lane t=0 takes lane 3's
+      // halos: neighbour lane's chunk (t-1); lane t=0 takes lane 3's
       const uint32_t H0g = __shfl_sync(0xffffffffu, t == 3 ? prevP1g : P0g, src);
       const uint32_t H0q = __shfl_sync(0xffffffffu, t == 3 ? prevP1q : P0q, src);
       const uint32_t H1g = __shfl_sync(0xffffffffu, t == 3 ? P0g : P1g, src);
       const uint32_t H1q = __shfl_sync(0xffffffffu, t == 3 ? P0q : P1q, src);
       prevP1g = P1g;
       prevP1q = P1q;
-      const uint32_t z0 = 0u;
 #pragma unroll
-      for (int cg = 0; cg < 2; ++cg) {
+      for (int cgi = 0; cgi < 2; ++cgi) {
         int zoff[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) zoff[nt] = zbase[nt] + zunit[nt] * (i * 32 + cg * 16);
-        const uint32_t Pg = cg ? P1g : P0g, Pq = cg ? P1q : P0q;
-        const uint32_t Hg = cg ? H1g : H0g, Hq = cg ? H1q : H0q;
-        uint32_t Mg0 = z0, Mq0 = z0, Mg1 = z0, Mq1 = z0, Mg2 = z0, Mq2 = z0;
+        for (int nt = 0; nt < NT; ++nt) zoff[nt] = zbase[nt] + zunit[nt] * (i * 32 + cgi * 16);
+        const uint32_t Pg = cgi ? P1g : P0g, Pq = cgi ? P1q : P0q;
+        const uint32_t Hg = cgi ? H1g : H0g, Hq = cgi ? H1q : H0q;
+        uint32_t Mg0 = 0u, Mq0 = 0u, Mg1 = 0u, Mq1 = 0u, Mg2 = 0u, Mq2 = 0u;
         if (BITS >= 2) {
-          Mg0 = cg ? cur[1].z : cur[1].x;
-          Mq0 = cg ? cur[1].w : cur[1].y;
+          Mg0 = cgi ? cur[1].z : cur[1].x;
+          Mq0 = cgi ? cur[1].w : cur[1].y;
         }
         if (BITS >= 3) {
-          Mg1 = cg ? cur[2].z : cur[2].x;
-          Mq1 = cg ? cur[2].w : cur[2].y;
+          Mg1 = cgi ? cur[2].z : cur[2].x;
+          Mq1 = cgi ? cur[2].w : cur[2].y;
         }
         if (BITS >= 4) {
-          Mg2 = cg ? cur[3].z : cur[3].x;
-          Mq2 = cg ? cur[3].w : cur[3].y;
+          Mg2 = cgi ? cur[3].z : cur[3].x;
+          Mq2 = cgi ? cur[3].w : cur[3].y;
         }
-        process_chunk<BITS, S, NT>(lut, lanew, zs, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
-      }
-      if (i + 1 < nunits) {
-#pragma unroll
-        for (int k = 0; k < BITS; ++k) cur[k] = nxt[k];
+        process_chunk<BITS, S, NT>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
       }
     }
+    if (!ok) s_fail = 1;  // copies never landed: outputs become NaN below
   }
 
-  // ---- epilogue ----
-  const int64_t row_g = rt * kTileRows + g, row_q = row_g + 8;
+  trace(5);
+  // ---- reduction ----
+  // red: [kw][rt*16][Bp] fp32; the CTA partial lands in slab 0.
+  const int Bp = NT * 8;
+  const int crows = p.rt * kTileRows;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int bn = nt * 8 + 2 * t + (e & 1);
+      const int r = rtl * kTileRows + g + ((e < 2) ? 0 : 8);
+      red[(kwi * crows + r) * Bp + bn] = acc[0][nt][e] + acc[1][nt][e];
+    }
+  }
+  __syncthreads();
+  if (p.kw > 1) {
+    for (int i = tid; i < crows * Bp; i += kThreads) {
+      float v = red[i];
+      for (int k = 1; k < p.kw; ++k) v += red[k * crows * Bp + i];
+      red[i] = v;
+    }
+    __syncthreads();
+  }
+  const int64_t row0 = (int64_t)blockIdx.x * crows;
+  trace(6);
+  if (s_fail) {
+    for (int i = tid; i < crows * Bp; i += kThreads) red[i] = __int_as_float(0x7fc00000);
+    __syncthreads();
+  }
   if (p.ksplit == 1) {
-    if (active) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int bn = nt * 8 + 2 * t + (e & 1);
-          const int64_t row = (e < 2) ? row_g : row_q;
-          if (bn < p.B && row < p.n) {
-            float v = acc[nt][e] * h2f_bits(p.scales[row]);
-            if (p.bias) v += h2f_bits(p.bias[row]);
-            store_from_float(p.y, (int64_t)bn * p.n + row, p.y_dtype, v);
-          }
-        }
+    for (int i = tid; i < crows * p.B; i += kThreads) {
+      const int bn = i / crows, r = i - bn * crows;
+      const int64_t row = row0 + r;
+      if (row < p.n) {
+        float v = red[r * Bp + bn] * h2f_bits(p.scales[row]);
+        if (p.bias) v += h2f_bits(p.bias[row]);
+        store_from_float(p.y, (int64_t)bn * p.n + row, p.y_dtype, v);
       }
     }
+    trace(7);
     return;
   }
-  if (active) {
+  if (p.cluster) {
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    const int rank = static_cast<int>(cl.block_rank());
+    // rank r finishes rows [r*crows/ks, (r+1)*crows/ks), summing ranks in order
+    const int ra = rank * crows / p.ksplit, rb = (rank + 1) * crows / p.ksplit;
+    const int nr = rb - ra;
+    const float* rp[kMaxCluster];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int k = 0; k < kMaxCluster; ++k) rp[k] = cl.map_shared_rank(red, k < p.ksplit ? k : 0);
+    for (int i = tid; i < nr * p.B; i += kThreads) {
+      const int bn = i / nr, r = ra + (i - bn * nr);
+      const int64_t row = row0 + r;
+      float part[kMaxCluster];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int bn = nt * 8 + 2 * t + (e & 1);
-        const int64_t row = (e < 2) ? row_g : row_q;
-        if (bn < p.B) p.partial[((int64_t)ks * p.B + bn) * p.n_pad + row] = acc[nt][e];
+      for (int k = 0; k < kMaxCluster; ++k) part[k] = k < p.ksplit ? rp[k][r * Bp + bn] : 0.f;
+      float v = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxCluster; ++k) v += part[k];
+      if (row < p.n) {
+        v *= h2f_bits(p.scales[row]);
+        if (p.bias) v += h2f_bits(p.bias[row]);
+        store_from_float(p.y, (int64_t)bn * p.n + row, p.y_dtype, v);
       }
     }
+    cl.sync();  // keep every CTA's shared memory alive until all reads are done
+    trace(7);
+    return;
+  }
+  // global split-K through the workspace; the last CTA of the row block reduces
+  for (int i = tid; i < crows * p.B; i += kThreads) {
+    const int bn = i / crows, r = i - bn * crows;
+    p.partial[((int64_t)ks * p.B + bn) * p.n_pad + row0 + r] = red[r * Bp + bn];
   }
   __threadfence();
   __syncthreads();
@@ -348,11 +634,9 @@ __global__ void __launch_bounds__(Cfg<BITS>::kWarps * 32) tcq_gemv_kernel(GemvPa
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const int64_t row0 = (int64_t)blockIdx.x * WARPS * kTileRows;
-  const int rows = WARPS * kTileRows;
-  for (int i = tid; i < rows * p.B; i += WARPS * 32) {
-    const int bn = i / rows;
-    const int64_t row = row0 + (i - bn * rows);
+  for (int i = tid; i < crows * p.B; i += kThreads) {
+    const int bn = i / crows;
+    const int64_t row = row0 + (i - bn * crows);
     if (row >= p.n) continue;
     float v = 0.f;
     for (int k = 0; k < p.ksplit; ++k) v += __ldcg(&p.partial[((int64_t)k * p.B + bn) * p.n_pad + row]);
@@ -361,20 +645,12 @@ __global__ void __launch_bounds__(Cfg<BITS>::kWarps * 32) tcq_gemv_kernel(GemvPa
     store_from_float(p.y, (int64_t)bn * p.n + row, p.y_dtype, v);
   }
   if (tid == 0) p.counters[blockIdx.x] = 0u;
+  trace(7);
 }
 
 // ---------------------------------------------------------------------------
 // launch configuration
 // ---------------------------------------------------------------------------
-struct Plan {
-  int warps;
-  int64_t row_blocks;
-  int units_k;
-  int ksplit;
-  size_t smem;
-  int64_t ws_counters, ws_z, ws_partial, ws_total;
-};
-
 int sm_count() {
   static std::mutex mu;
   static int cache[64] = {0};
@@ -390,35 +666,108 @@ int sm_count() {
   return cache[dev];
 }
 
-inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+// TP_DEBUG_PLAN=1 prints every launch configuration to stderr.
+bool debug_plans() {
+  static const bool on = [] {
+    const char* e = getenv("TP_DEBUG_PLAN");
+    return e && *e && *e != '0';
+  }();
+  return on;
+}
 
-Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int sms) {
-  Plan pl{};
-  const int64_t Bc = B < kMaxBatchPerLaunch ? B : kMaxBatchPerLaunch;
-  pl.warps = bits == 4 ? Cfg<4>::kWarps : Cfg<3>::kWarps;
+inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+inline uint32_t align128(uint32_t v) { return (v + 127) / 128 * 128; }
+
+struct Plan {
+  int rt, kw, ksplit, cluster;
+  int64_t row_blocks;
+  int units_k;
+  int zrows_per_pass;
+  int slots;
+  bool fused_rotation;
+  uint32_t w_off, z_off, scratch_off, red_off;
+  size_t smem;
+  int64_t ws_z, ws_partial, ws_total;
+};
+
+// Shared-memory carve-up of a configuration: pair table, activation slice,
+// fp32 FWHT scratch and the reduction slabs.
+void carve(Plan& pl, int bits, int64_t Bc, int slice_units, int64_t block) {
+  const int Bp = static_cast<int>((Bc + 7) / 8) * 8;
+  pl.w_off = bits == 4 ? Cfg<4>::kLutBytes : Cfg<3>::kLutBytes;
+  pl.z_off = pl.w_off + static_cast<uint32_t>(kWarps * pl.slots * 512 * bits);
+  const uint32_t zbytes = static_cast<uint32_t>(Bc * slice_units * kUnitCols * 2 + 64);
+  pl.scratch_off = align128(pl.z_off + zbytes);
+  uint32_t scratch = 0;
+  pl.zrows_per_pass = 1;
+  if (pl.fused_rotation) {
+    // Hadamard blocks overlapping a slice of `cols` columns that starts on a
+    // 256-column boundary: exactly the slice when block <= 256, otherwise at
+    // most ceil(cols / block) + 1 whole blocks.
+    const int64_t cols = (int64_t)slice_units * kUnitCols;
+    const int64_t per_row = block <= kUnitCols ? cols : ((cols + block - 1) / block + 1) * block;
+    pl.zrows_per_pass = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(Bc, kScratchFloats / per_row)));
+    scratch = static_cast<uint32_t>(pl.zrows_per_pass * per_row * 4);
+  }
+  pl.red_off = align128(pl.scratch_off + scratch);
+  const uint32_t red = static_cast<uint32_t>(pl.kw * pl.rt * kTileRows * Bp * 4);
+  pl.smem = align128(pl.red_off + red);
+}
+
+Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms) {
+  Plan best{};
+  const int64_t Bc = std::min<int64_t>(B, kMaxBatchPerLaunch);
   const int64_t n_pad = pad_to(n, kTileRows), d_pad = pad_to(d, kUnitCols);
   const int64_t row_tiles = n_pad / kTileRows;
-  pl.row_blocks = (row_tiles + pl.warps - 1) / pl.warps;
-  pl.units_k = static_cast<int>(d_pad / kUnitCols);
-  const int ctas_per_sm = bits == 4 ? 1 : 3;
-  const int64_t target = (int64_t)sms * ctas_per_sm;
-  int64_t ks = (target + pl.row_blocks - 1) / pl.row_blocks;
-  // keep the activation slice in shared memory modest: <= 64 KB
-  const int64_t max_units_smem = std::max<int64_t>(1, (64 * 1024) / (Bc * 512));
-  const int64_t min_ks = (pl.units_k + max_units_smem - 1) / max_units_smem;
-  ks = std::max(ks, min_ks);
-  ks = std::min<int64_t>(ks, 32);
-  ks = std::min<int64_t>(ks, pl.units_k);
-  ks = std::max<int64_t>(ks, 1);
-  pl.ksplit = static_cast<int>(ks);
-  const int64_t slice_units = (pl.units_k + pl.ksplit - 1) / pl.ksplit;
-  const int lut = bits == 4 ? Cfg<4>::kLutBytes : Cfg<3>::kLutBytes;
-  pl.smem = static_cast<size_t>(lut + (Bc * slice_units * 32 + 4) * 16);
-  pl.ws_counters = kCounterBytes;
-  pl.ws_z = align256(Bc * d_pad * 2);
-  pl.ws_partial = pl.ksplit > 1 ? align256((int64_t)pl.ksplit * Bc * n_pad * 4) : 0;
-  pl.ws_total = pl.ws_counters + pl.ws_z + pl.ws_partial;
-  return pl;
+  const int units_k = static_cast<int>(d_pad / kUnitCols);
+  const bool fused = block <= kMaxFusedBlock;
+  int64_t best_score = -1;
+  for (int rt : {8, 4, 2, 1}) {
+    const int kw = kWarps / rt;
+    const int64_t row_blocks = (row_tiles + rt - 1) / rt;
+    if (row_blocks > kMaxRowBlocks) continue;
+    for (int ks = 1; ks <= std::min(32, units_k); ++ks) {
+      const int slice = (units_k + ks - 1) / ks;
+      if (slice < kw && !(ks == 1 && rt == 8)) continue;  // every warp gets >= 1 unit
+      Plan pl{};
+      pl.rt = rt;
+      pl.kw = kw;
+      pl.ksplit = ks;
+      pl.cluster = ks > 1 && ks <= kMaxCluster ? 1 : 0;
+      pl.row_blocks = row_blocks;
+      pl.units_k = units_k;
+      pl.fused_rotation = fused;
+      // stage every unit of a warp when it fits, else a ring of >= 2 units
+      const int warp_units = (slice + kw - 1) / kw;
+      pl.slots = std::min(warp_units, kMaxSlots);
+      carve(pl, bits, Bc, slice, block);
+      while (pl.smem > kMaxDynSmem && pl.slots > 2) {
+        --pl.slots;
+        carve(pl, bits, Bc, slice, block);
+      }
+      if (pl.smem > kMaxDynSmem) continue;
+      // registers (<= 128 per thread, launch bound of 2 CTAs) and shared memory
+      // registers (<= 128 per thread, launch bound of 2 CTAs) and shared memory
+      const int per_sm = std::max(1, std::min<int>((228 * 1024) / (int)(pl.smem + 3072), 2));
+      const int64_t cap = (int64_t)sms * per_sm;
+      const int64_t ctas = row_blocks * ks;
+      // fill one wave with as many CTAs as possible; penalise extra waves,
+      // the global (non-cluster) reduction and larger splits
+      const int64_t waves = (ctas + cap - 1) / cap;
+      int64_t score = (ctas <= cap ? ctas : cap / waves) * 64;
+      if (ks > kMaxCluster) score -= 32 * 64;
+      score -= ks;
+      if (pl.slots < warp_units) score -= 16 * 64;  // prefer everything in flight at once
+      if (score > best_score) {
+        best_score = score;
+        best = pl;
+      }
+    }
+  }
+  best.ws_z = best.fused_rotation ? 0 : align256(Bc * d_pad * 2);
+  best.ws_partial = (best.ksplit > 1 && !best.cluster) ? align256((int64_t)best.ksplit * Bc * n_pad * 4) : 0;
+  best.ws_total = kCounterBytes + best.ws_z + best.ws_partial;
+  return best;
 }
 
 template <int BITS, int S, int NT>
@@ -426,15 +775,32 @@ tp_status launch_gemv_t(const GemvParams& p, const Plan& pl, cudaStream_t stream
   auto kern = tcq_gemv_kernel<BITS, S, NT>;
   static int smem_set[64] = {0};
   if (tp_status s = ensure_smem(kern, pl.smem, smem_set, "cudaFuncSetAttribute(gemv)")) return s;
-  dim3 grid(static_cast<unsigned>(pl.row_blocks), static_cast<unsigned>(pl.ksplit));
-  kern<<<grid, Cfg<BITS>::kWarps * 32, pl.smem, stream>>>(p);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.row_blocks), static_cast<unsigned>(pl.ksplit), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (pl.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = static_cast<unsigned>(pl.ksplit);
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  TP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p), "tcq_gemv_kernel launch");
   return check_launch("tcq_gemv_kernel");
 }
 
 template <int BITS, int S>
 tp_status launch_gemv_nt(const GemvParams& p, const Plan& pl, cudaStream_t stream) {
-  const int nt = (p.B + 7) / 8;
-  switch (nt) {
+  switch ((p.B + 7) / 8) {
     case 1: return launch_gemv_t<BITS, S, 1>(p, pl, stream);
     case 2: return launch_gemv_t<BITS, S, 2>(p, pl, stream);
     case 3: return launch_gemv_t<BITS, S, 3>(p, pl, stream);
@@ -508,7 +874,11 @@ __global__ void gemv_v2_kernel(const float* __restrict__ z, const uint8_t* __res
 
 extern "C" int64_t tp_gemv_workspace_bytes(int64_t B, int64_t n, int64_t d, int bits) {
   if (B < 1 || n < 1 || d < 1 || bits < 1 || bits > 4) return -1;
-  return make_plan(B, n, d, bits, sm_count()).ws_total;
+  // the plan depends on the Hadamard block only through the fused/unfused
+  // choice; size for the unfused case so any block fits
+  Plan pl = make_plan(B, n, d, bits, int64_t(1) << 30, sm_count());
+  Plan pf = make_plan(B, n, d, bits, 1, sm_count());
+  return std::max(pl.ws_total, pf.ws_total);
 }
 
 extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot_scale, const uint8_t* tcq_stream,
@@ -523,47 +893,81 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
   if (!aligned(tcq_stream, 16)) return fail(TP_ERR_ALIGN, "tp_tcq_gemv: stream must be 16-byte aligned");
   if (B == 0 || n == 0) return clear_ok();
   if (d == 0) return fail(TP_ERR_ARG, "tp_tcq_gemv: d must be positive");
-  const Plan pl = make_plan(B, n, d, bits, sm_count());
-  if (pl.row_blocks > kMaxRowBlocks)
-    return fail(TP_ERR_UNSUPPORTED, "tp_tcq_gemv: n=%lld exceeds the supported maximum row count", (long long)n);
-  if (!workspace || workspace_bytes < pl.ws_total)
-    return fail(TP_ERR_WORKSPACE, "tp_tcq_gemv: workspace of %lld bytes required (got %lld)", (long long)pl.ws_total,
+  if (block < 1 || (block & (block - 1)) || d % block)
+    return fail(TP_ERR_ARG, "block must be a power of two dividing d (d=%lld, block=%lld)", (long long)d,
+                (long long)block);
+  if (block > kMaxRotateBlock)
+    return fail(TP_ERR_UNSUPPORTED, "Hadamard block %lld exceeds the supported maximum %d", (long long)block,
+                kMaxRotateBlock);
+  const int sms = sm_count();
+  const Plan pl = make_plan(B, n, d, bits, block, sms);
+  if (pl.row_blocks == 0 || pl.smem == 0)
+    return fail(TP_ERR_UNSUPPORTED, "tp_tcq_gemv: no launch configuration for n=%lld d=%lld", (long long)n,
+                (long long)d);
+  const int64_t need = tp_gemv_workspace_bytes(B, n, d, bits);
+  if (!workspace || workspace_bytes < need)
+    return fail(TP_ERR_WORKSPACE, "tp_tcq_gemv: workspace of %lld bytes required (got %lld)", (long long)need,
                 (long long)workspace_bytes);
   if (!aligned(workspace, 256)) return fail(TP_ERR_ALIGN, "tp_tcq_gemv: workspace must be 256-byte aligned");
   cudaStream_t st = as_stream(stream);
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   const int64_t d_pad = pad_to(d, kUnitCols), n_pad = pad_to(n, kTileRows);
   const size_t xel = x_dtype == TP_F32 ? 4 : 2, yel = y_dtype == TP_F32 ? 4 : 2;
+  int lg = 0;
+  while ((int64_t(1) << lg) < block) ++lg;
   for (int64_t b0 = 0; b0 < B; b0 += kMaxBatchPerLaunch) {
     const int64_t Bc = std::min<int64_t>(kMaxBatchPerLaunch, B - b0);
-    const Plan pc = make_plan(Bc, n, d, bits, sm_count());
-    RotateArgs ra{};
-    ra.x = static_cast<const unsigned char*>(x) + b0 * d * xel;
-    ra.x_dtype = x_dtype;
-    ra.scale = rot_scale;
-    ra.z = ws + pl.ws_counters;
-    ra.z_dtype = TP_F16;
-    ra.d = d;
-    ra.d_pad = d_pad;
-    ra.block = block;
-    ra.mode = 2;
-    if (tp_status s = launch_rotate(ra, Bc, st)) return s;
+    const Plan pc = make_plan(Bc, n, d, bits, block, sms);
+    const void* xc = static_cast<const unsigned char*>(x) + b0 * d * xel;
     GemvParams p{};
+    if (!pc.fused_rotation) {
+      RotateArgs ra{};
+      ra.x = xc;
+      ra.x_dtype = x_dtype;
+      ra.scale = rot_scale;
+      ra.z = ws + kCounterBytes;
+      ra.z_dtype = TP_F16;
+      ra.d = d;
+      ra.d_pad = d_pad;
+      ra.block = block;
+      ra.mode = 2;
+      if (tp_status s = launch_rotate(ra, Bc, st)) return s;
+      p.zperm = reinterpret_cast<const uint4*>(ws + kCounterBytes);
+    }
     p.stream = reinterpret_cast<const uint4*>(tcq_stream);
     p.scales = scales;
     p.bias = bias;
     p.codebook = codebook;
-    p.zperm = reinterpret_cast<const uint4*>(ws + pl.ws_counters);
+    p.x = xc;
+    p.rot_scale = rot_scale;
     p.y = static_cast<unsigned char*>(y) + b0 * n * yel;
-    p.partial = reinterpret_cast<float*>(ws + pl.ws_counters + pl.ws_z);
+    p.partial = reinterpret_cast<float*>(ws + kCounterBytes + pc.ws_z);
     p.counters = reinterpret_cast<unsigned*>(ws);
+    p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
     p.B = static_cast<int>(Bc);
     p.n = n;
     p.n_pad = n_pad;
+    p.d = d;
     p.d_pad = d_pad;
     p.units_k = pc.units_k;
+    p.block = static_cast<int>(block);
+    p.lg_block = lg;
+    p.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(block)));
+    p.rt = pc.rt;
+    p.kw = pc.kw;
     p.ksplit = pc.ksplit;
+    p.cluster = pc.cluster;
+    p.zrows_per_pass = pc.zrows_per_pass;
+    p.slots = pc.slots;
+    p.w_off = pc.w_off;
+    p.z_off = pc.z_off;
+    p.scratch_off = pc.scratch_off;
+    p.red_off = pc.red_off;
+    if (debug_plans())
+      fprintf(stderr, "tp_tcq_gemv n=%lld d=%lld B=%lld bits=%d: rt=%d kw=%d ksplit=%d cluster=%d slots=%d "
+              "smem=%zu grid=%lldx%d fused=%d\n", (long long)n, (long long)d, (long long)Bc, bits, pc.rt, pc.kw,
+              pc.ksplit, pc.cluster, pc.slots, pc.smem, (long long)pc.row_blocks, pc.ksplit, (int)pc.fused_rotation);
     if (tp_status s = launch_gemv(p, pc, bits, n_states, st)) return s;
   }
   return clear_ok();
@@ -594,3 +998,9 @@ extern "C" tp_status tp_gemv_v2(const float* z, const uint8_t* path_packed, cons
   }
   return clear_ok();
 }
+
+#ifdef TP_TRACE
+extern "C" TP_API int tp_trace_read(unsigned long long* host, int ctas) {
+  return (int)cudaMemcpyFromSymbol(host, g_trace, (size_t)ctas * 16 * sizeof(unsigned long long));
+}
+#endif
