@@ -201,9 +201,7 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // The codebook (<= 32 fp16) sits one entry per lane and is read by shuffle;
 // each warp instruction stores four 128-byte table rows.
 template <int BITS>
-__device__ __forceinline__ void build_lut(unsigned char* lut, const uint16_t* __restrict__ cb, int warp, int lane) {
-  constexpr int kCb = 1 << (BITS + 1);
-  const uint32_t cbv = lane < kCb ? cb[lane] : 0u;
+__device__ __forceinline__ void build_lut(unsigned char* lut, uint32_t cbv, int warp, int lane) {
   const int row = lane >> 3, col = lane & 7;
   constexpr int kEntries = BITS <= 3 ? 256 : 1024;
   for (int e0 = warp * 4; e0 < kEntries; e0 += kWarps * 4) {
@@ -375,12 +373,10 @@ __device__ void rotate_slice(const GemvParams& p, int64_t c0, int ncols, __half*
     return;
   }
   if (vend < c1) {  // zero the slice columns past d
-    const int nz = static_cast<int>(c1 - (vend > c0 ? vend : c0));
-    for (int i = tid; i < B * nz; i += kThreads) {
-      const int b = i / nz;
-      const int lc = static_cast<int>(c1 - nz - c0) + (i - b * nz);
-      zs[b * ncols + (lc & ~31) + zperm_pos(lc & 31)] = __float2half_rn(0.f);
-    }
+    const int lc0 = static_cast<int>((vend > c0 ? vend : c0) - c0);
+    for (int b = 0; b < B; ++b)
+      for (int lc = lc0 + tid; lc < ncols; lc += kThreads)
+        zs[b * ncols + (lc & ~31) + zperm_pos(lc & 31)] = __float2half_rn(0.f);
   }
   if (c0 >= p.d) return;
   const int64_t blk = p.block;
@@ -389,11 +385,10 @@ __device__ void rotate_slice(const GemvParams& p, int64_t c0, int ncols, __half*
   const int span = static_cast<int>(s1 - s0);
   for (int b0 = 0; b0 < B; b0 += p.zrows_per_pass) {
     const int rows = B - b0 < p.zrows_per_pass ? B - b0 : p.zrows_per_pass;
-    for (int i = tid; i < rows * span; i += kThreads) {
-      const int rr = i / span, c = i - rr * span;
-      const int64_t col = s0 + c;
-      scratch[i] = load_as_float(p.x, (int64_t)(b0 + rr) * p.d + col, p.x_dtype) * h2f_bits(p.rot_scale[col]);
-    }
+    for (int rr = 0; rr < rows; ++rr)
+      for (int c = tid; c < span; c += kThreads)
+        scratch[rr * span + c] =
+            load_as_float(p.x, (int64_t)(b0 + rr) * p.d + s0 + c, p.x_dtype) * h2f_bits(p.rot_scale[s0 + c]);
     __syncthreads();
     trace(8);
     if (blk <= 1024) {
@@ -404,12 +399,11 @@ __device__ void rotate_slice(const GemvParams& p, int64_t c0, int ncols, __half*
       fwht_shared(scratch, rows * span, p.lg_block);
     }
     trace(9);
-    for (int i = tid; i < rows * ncols; i += kThreads) {
-      const int rr = i / ncols, lc = i - rr * ncols;
-      const int64_t col = c0 + lc;
-      if (col < vend) zs[(b0 + rr) * ncols + (lc & ~31) + zperm_pos(lc & 31)] =
-          __float2half_rn(scratch[rr * span + (int)(col - s0)] * p.norm);
-    }
+    const int nvalid = static_cast<int>(vend - c0), soff = static_cast<int>(c0 - s0);
+    for (int rr = 0; rr < rows; ++rr)
+      for (int lc = tid; lc < nvalid; lc += kThreads)
+        zs[(b0 + rr) * ncols + (lc & ~31) + zperm_pos(lc & 31)] =
+            __float2half_rn(scratch[rr * span + soff + lc] * p.norm);
     __syncthreads();
   }
 }
@@ -436,6 +430,8 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
   const bool active = rt * kTileRows < p.n_pad;
 
   trace(0);
+  // codebook entry of this lane (<= 32 levels), fetched before anything else
+  const uint32_t cbv = lane < (1 << (BITS + 1)) ? p.codebook[lane] : 0u;
   // the next kernel in the stream may start its own prologue now; it waits
   // for this grid's completion before touching our outputs
   pdl_trigger();
@@ -466,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
     prevP1q = pv.w;
   }
   trace(1);
-  build_lut<BITS>(lut, p.codebook, warp, lane);
+  build_lut<BITS>(lut, cbv, warp, lane);
   trace(2);
 
   // ---- activations: wait for the producer of x, then rotate our slice ----
@@ -499,9 +495,10 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
     const uint32_t lanew = BITS <= 3 ? (uint32_t)lane * 4u : (uint32_t)lane * 4u * 0x10001u;
     const int src = (lane & ~3) | ((t + 3) & 3);
     bool ok = true;
+    int s = 0;             // ring slot of unit i
+    unsigned parity = 0u;  // mbarrier phase parity of that slot
     for (int i = 0; i < nunits; ++i) {
-      const int s = i % p.slots;
-      if (!mbar_wait(&s_bar[warp][s], (unsigned)(i / p.slots) & 1u)) {
+      if (!mbar_wait(&s_bar[warp][s], parity)) {
         ok = false;
         break;
       }
@@ -544,6 +541,10 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
           Mq2 = cgi ? cur[3].w : cur[3].y;
         }
         process_chunk<BITS, S, NT>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
+      }
+      if (++s == p.slots) {
+        s = 0;
+        parity ^= 1u;
       }
     }
     if (!ok) s_fail = 1;  // copies never landed: outputs become NaN below
@@ -721,7 +722,11 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms
   const int64_t row_tiles = n_pad / kTileRows;
   const int units_k = static_cast<int>(d_pad / kUnitCols);
   const bool fused = block <= kMaxFusedBlock;
-  int64_t best_score = -1;
+  // Pick the configuration with the lowest modelled time: waves of CTAs
+  // times a fixed per-wave latency, plus the bytes over the bandwidth that
+  // the SMs in use can pull with the weight bytes they keep in flight.
+  const double total_bytes = (double)n_pad * d_pad * bits / 8.0;
+  double best_t = 1e30;
   for (int rt : {8, 4, 2, 1}) {
     const int kw = kWarps / rt;
     const int64_t row_blocks = (row_tiles + rt - 1) / rt;
@@ -729,38 +734,41 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms
     for (int ks = 1; ks <= std::min(32, units_k); ++ks) {
       const int slice = (units_k + ks - 1) / ks;
       if (slice < kw && !(ks == 1 && rt == 8)) continue;  // every warp gets >= 1 unit
-      Plan pl{};
-      pl.rt = rt;
-      pl.kw = kw;
-      pl.ksplit = ks;
-      pl.cluster = ks > 1 && ks <= kMaxCluster ? 1 : 0;
-      pl.row_blocks = row_blocks;
-      pl.units_k = units_k;
-      pl.fused_rotation = fused;
-      // stage every unit of a warp when it fits, else a ring of >= 2 units
       const int warp_units = (slice + kw - 1) / kw;
-      pl.slots = std::min(warp_units, kMaxSlots);
-      carve(pl, bits, Bc, slice, block);
-      while (pl.smem > kMaxDynSmem && pl.slots > 2) {
-        --pl.slots;
+      for (int slots : {warp_units, 4, 3, 2}) {
+        if (slots > warp_units || slots > kMaxSlots || slots < 1) continue;
+        Plan pl{};
+        pl.rt = rt;
+        pl.kw = kw;
+        pl.ksplit = ks;
+        pl.cluster = ks > 1 && ks <= kMaxCluster ? 1 : 0;
+        pl.row_blocks = row_blocks;
+        pl.units_k = units_k;
+        pl.fused_rotation = fused;
+        pl.slots = slots;
         carve(pl, bits, Bc, slice, block);
-      }
-      if (pl.smem > kMaxDynSmem) continue;
-      // registers (<= 128 per thread, launch bound of 2 CTAs) and shared memory
-      // registers (<= 128 per thread, launch bound of 2 CTAs) and shared memory
-      const int per_sm = std::max(1, std::min<int>((228 * 1024) / (int)(pl.smem + 3072), 2));
-      const int64_t cap = (int64_t)sms * per_sm;
-      const int64_t ctas = row_blocks * ks;
-      // fill one wave with as many CTAs as possible; penalise extra waves,
-      // the global (non-cluster) reduction and larger splits
-      const int64_t waves = (ctas + cap - 1) / cap;
-      int64_t score = (ctas <= cap ? ctas : cap / waves) * 64;
-      if (ks > kMaxCluster) score -= 32 * 64;
-      score -= ks;
-      if (pl.slots < warp_units) score -= 16 * 64;  // prefer everything in flight at once
-      if (score > best_score) {
-        best_score = score;
-        best = pl;
+        if (pl.smem > kMaxDynSmem) continue;
+        // registers (<= 128 per thread, launch bound of 2 CTAs) and shared memory
+        const int per_sm = std::max(1, std::min<int>((228 * 1024) / (int)(pl.smem + 3072), 2));
+        const int64_t cap = (int64_t)sms * per_sm;
+        const int64_t ctas = row_blocks * ks;
+        const int64_t waves = (ctas + cap - 1) / cap;
+        // CTAs spread over SMs before doubling up
+        const double sm_used = (double)std::min<int64_t>(ctas, sms);
+        const int64_t per_sm_used = std::min<int64_t>(per_sm, (std::min(ctas, cap) + sms - 1) / sms);
+        const double inflight = (double)per_sm_used * kWarps * slots * 512.0 * bits;
+        const double t_mem = total_bytes / (6.5e12 * (sm_used / sms) * std::min(1.0, inflight / (72.0 * 1024)));
+        // issue-limited decode: ~2.2 lane instructions per weight, half the
+        // issue rate at 8 resident warps per SM, full rate from 16
+        const double issue = std::min(1.0, per_sm_used * kWarps / 16.0);
+        const double t_cmp = total_bytes * 8.0 / bits * 2.2 / (sm_used * 128.0 * issue * 1.9e9);
+        double t = waves * 4e-6 + std::max(t_mem, t_cmp);
+        if (ks > kMaxCluster) t += 1.5e-6;  // global reduction through the workspace
+        t += ks * 1e-8;                     // prefer fewer splits on ties
+        if (t < best_t) {
+          best_t = t;
+          best = pl;
+        }
       }
     }
   }
