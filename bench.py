@@ -337,6 +337,74 @@ def run_gpu(args) -> dict | None:
     return out
 
 
+def random_linear(n: int, d: int, bits: int, device, seed: int, cb=None):
+    """One PackedTCQLinear with seeded random trellis streams (GPU-generated)."""
+    import torch
+
+    from turbopress_b200 import PackedTCQLinear
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    if cb is None:
+        cb = torch.from_numpy(codebook(bits)).to(device)
+    payload = {
+        "format": 2, "n": n, "d": d, "bits": bits, "n_states": 64, "block": d & -d, "seed": seed,
+        "path_packed": torch.randint(0, 256, (n, -(-d // 8)), generator=g, dtype=torch.uint8, device=device),
+        "member_packed": torch.randint(0, 256, (n, -(-d * (bits - 1) // 8)), generator=g, dtype=torch.uint8,
+                                       device=device) if bits > 1 else None,
+        "scales": ((torch.rand(n, generator=g, device=device) * 0.5 + 0.75) / math.sqrt(d)).half(),
+        "signs_packed": torch.randint(0, 256, (1, -(-d // 8)), generator=g, dtype=torch.uint8, device=device),
+        "inv_equil": (torch.rand(d, generator=g, device=device) * 0.4 + 0.8).half(),
+        "codebook": cb.clone(),
+        "bias": None,
+    }
+    return PackedTCQLinear(payload, mode="cuda")
+
+
+def run_gemv(args) -> dict:
+    """Standalone packed GEMVs (BASELINE config 3 shapes by default): per shape,
+    `copies` distinct weight sets in one CUDA graph (so each launch streams its
+    weights from HBM), timed with CUDA events; --once runs one call per shape
+    (for profiler captures)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    res = {}
+    for shp in args.shapes.split(","):
+        n, d = map(int, shp.lower().split("x"))
+        copies = 1 if args.once else max(1, min(args.copies, int(2e9 // max(1, n * d * args.bits // 8))))
+        mods = [random_linear(n, d, args.bits, dev, seed=c) for c in range(copies)]
+        x = torch.randn(args.batch, d, device=dev, dtype=torch.float16)
+        if args.once:
+            mods[0](x)
+            torch.cuda.synchronize()
+            continue
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.no_grad(), torch.cuda.stream(s):
+            for m in mods:
+                m(x)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for m in mods:
+                    m(x)
+            for _ in range(max(args.warmup, 3)):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(s)
+            e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps / copies
+        nbytes = gemv_bytes(n, d, args.bits, args.batch)
+        res[shp] = {"us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1), "MB": round(nbytes / 1e6, 2),
+                    "copies": copies}
+        del mods, graph
+        torch.cuda.empty_cache()
+    return {"workload": "gemv", "bits": args.bits, "batch": args.batch, "shapes": res}
+
+
 def run_reference(args) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -378,7 +446,16 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+                    help="decode: the contract line (Qwen3-4B decode step); gemv: standalone GEMV table")
+    ap.add_argument("--shapes", default="14336x4096,4096x14336,4096x4096,1024x4096",
+                    help="gemv workload: comma-separated NxD (out x in) shapes")
+    ap.add_argument("--copies", type=int, default=16, help="gemv workload: distinct weight sets per shape")
+    ap.add_argument("--once", action="store_true", help="gemv workload: one call per shape (profiling)")
     args = ap.parse_args()
+    if args.workload == "gemv" and args.impl != "reference":
+        print(json.dumps(run_gemv(args)), flush=True)
+        return
     out = run_reference(args) if args.impl == "reference" else run_gpu(args)
     if out is not None:
         print(json.dumps(out), flush=True)

@@ -11,8 +11,7 @@
  *     owned and allocated by the caller; no entry point allocates device
  *     memory, synchronizes the device or the stream, or keeps a pointer
  *     after it returns.  Every launch is enqueued on `stream` (a
- *     cudaStream_t passed as void*, NULL = legacy default stream), so all
- *     calls can be captured into a CUDA graph.
+ *     cudaStream_t passed as void*, NULL = legacy default stream).
  *   - Half-precision values travel as uint16_t bit patterns (IEEE fp16).
  *   - n = out_features, d = in_features, bits = payload bits per weight,
  *     n_states = trellis states S in {4, 8, 16, 64}.
