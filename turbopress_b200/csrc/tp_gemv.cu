@@ -721,7 +721,7 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms
   const int64_t n_pad = pad_to(n, kTileRows), d_pad = pad_to(d, kUnitCols);
   const int64_t row_tiles = n_pad / kTileRows;
   const int units_k = static_cast<int>(d_pad / kUnitCols);
-  const bool fused = block <= kMaxFusedBlock;
+  const bool can_fuse = block <= kMaxFusedBlock;
   // Pick the configuration with the lowest modelled time: waves of CTAs
   // times a fixed per-wave latency, plus the bytes over the bandwidth that
   // the SMs in use can pull with the weight bytes they keep in flight.
@@ -735,8 +735,10 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms
       const int slice = (units_k + ks - 1) / ks;
       if (slice < kw && !(ks == 1 && rt == 8)) continue;  // every warp gets >= 1 unit
       const int warp_units = (slice + kw - 1) / kw;
+      for (int fuse = can_fuse ? 1 : 0; fuse >= 0; --fuse)
       for (int slots : {warp_units, 4, 3, 2}) {
         if (slots > warp_units || slots > kMaxSlots || slots < 1) continue;
+        const bool fused = fuse != 0;
         Plan pl{};
         pl.rt = rt;
         pl.kw = kw;
@@ -763,6 +765,13 @@ Plan make_plan(int64_t B, int64_t n, int64_t d, int bits, int64_t block, int sms
         const double issue = std::min(1.0, per_sm_used * kWarps / 16.0);
         const double t_cmp = total_bytes * 8.0 / bits * 2.2 / (sm_used * 128.0 * issue * 1.9e9);
         double t = waves * 4e-6 + std::max(t_mem, t_cmp);
+        // rotation: in every CTA over the Hadamard blocks its slice touches,
+        // or once by a separate (PDL-overlapped) launch into the workspace
+        const int64_t span = block <= kUnitCols ? (int64_t)slice * kUnitCols
+                                                : ((int64_t)slice * kUnitCols + block - 1) / block * block;
+        int lgb = 0;
+        while ((int64_t(1) << lgb) < block) ++lgb;
+        t += fused ? (double)Bc * span * (lgb + 6) / (0.5 * 128.0 * 1.9e9) + 0.5e-6 : 2.5e-6;
         if (ks > kMaxCluster) t += 1.5e-6;  // global reduction through the workspace
         t += ks * 1e-8;                     // prefer fewer splits on ties
         if (t < best_t) {
@@ -882,11 +891,10 @@ __global__ void gemv_v2_kernel(const float* __restrict__ z, const uint8_t* __res
 
 extern "C" int64_t tp_gemv_workspace_bytes(int64_t B, int64_t n, int64_t d, int bits) {
   if (B < 1 || n < 1 || d < 1 || bits < 1 || bits > 4) return -1;
-  // the plan depends on the Hadamard block only through the fused/unfused
-  // choice; size for the unfused case so any block fits
-  Plan pl = make_plan(B, n, d, bits, int64_t(1) << 30, sm_count());
-  Plan pf = make_plan(B, n, d, bits, 1, sm_count());
-  return std::max(pl.ws_total, pf.ws_total);
+  // Upper bound over every launch plan: counters, pre-rotated activations and
+  // partial sums for the largest split along K (32).
+  const int64_t Bc = std::min<int64_t>(B, kMaxBatchPerLaunch);
+  return kCounterBytes + align256(Bc * pad_to(d, kUnitCols) * 2) + align256(32 * Bc * pad_to(n, kTileRows) * 4);
 }
 
 extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot_scale, const uint8_t* tcq_stream,
@@ -926,6 +934,9 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
   for (int64_t b0 = 0; b0 < B; b0 += kMaxBatchPerLaunch) {
     const int64_t Bc = std::min<int64_t>(kMaxBatchPerLaunch, B - b0);
     const Plan pc = make_plan(Bc, n, d, bits, block, sms);
+    if (pc.ws_total > need)
+      return fail(TP_ERR_WORKSPACE, "tp_tcq_gemv: plan needs %lld workspace bytes (bound %lld)",
+                  (long long)pc.ws_total, (long long)need);
     const void* xc = static_cast<const unsigned char*>(x) + b0 * d * xel;
     GemvParams p{};
     if (!pc.fused_rotation) {
