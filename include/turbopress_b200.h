@@ -190,6 +190,54 @@ TP_API tp_status tp_tcq_gemv_noalloc(const void* x, int x_dtype, const uint16_t*
                                      int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block,
                                      int bits, int n_states, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Persistent decode engine: a chain of packed linears in ONE launch.
+ *
+ * Every SM keeps one CTA resident for the whole program, builds the pair
+ * table once, and streams each warp's weight units through a bulk-copy ring
+ * that runs ahead across op boundaries, so later layers' weights load while
+ * earlier ones wait for their activations.  An op waits (bounded) until
+ * every CTA has finished the op that produces its input; partial outputs
+ * are scaled and accumulated with fp32 atomics (order not fixed, so results
+ * may differ from tp_tcq_gemv in the last bits).  All ops share one bit
+ * width, state count and codebook; batch <= 4; Hadamard blocks 1..8192.
+ * Replaces a sequence of PackedTCQLinear.forward calls in mode "triton"
+ * (turbopress/runtime.py:312-334) chained by their activations.
+ * ---------------------------------------------------------------------- */
+typedef struct tp_engine_op {
+  const uint8_t* tcq_stream;  /* native stream of the layer                      */
+  const uint16_t* scales;     /* fp16 [n]                                         */
+  const uint16_t* bias;       /* fp16 [n] or NULL                                 */
+  const uint16_t* rot_scale;  /* fp16 [d]                                         */
+  const void* x;              /* input activations [B][d] (x_dtype)               */
+  float* y;                   /* fp32 output [B][n]; must be zero before each run */
+  int64_t n, d;
+  int32_t block;              /* Hadamard block of the layer                      */
+  int32_t x_dtype;            /* TP_F16 / TP_BF16 / TP_F32                        */
+  int32_t dep;                /* index of the op whose y is this op's x, or -1    */
+  int32_t reserved;
+} tp_engine_op;
+
+/* Bytes of the program image for n_ops ops. */
+TP_API int64_t tp_engine_image_bytes(int n_ops);
+
+/* Build the program image in HOST memory (no device work): validates the
+ * ops and derives the launch layout for the current device.  The caller
+ * copies the image to a device buffer of the same size (16-byte aligned)
+ * and passes both copies to tp_engine_run.  codebook: fp16 device pointer
+ * shared by every op. */
+TP_API tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, int bits, int n_states,
+                                 const uint16_t* codebook, void* image, int64_t image_bytes);
+
+/* Bytes of the counter block (n_ops + 1 words); zero it before each run.
+ * After a run, word n_ops is non-zero if a wait timed out. */
+TP_API int64_t tp_engine_counter_bytes(int n_ops);
+
+/* Run the program on `stream` (image_dev: device copy; image_host: the
+ * host image it was copied from). */
+TP_API tp_status tp_engine_run(const void* image_dev, const void* image_host, unsigned* counters,
+                               void* stream);
+
 /* Reference-order GEMV straight from the format-v2 streams, any bits in 1..7:
  * y[B, n] = z[B, d] @ decode_rows^T (+ bias), z fp32 rotated activations.
  * Used for payloads the native stream does not cover (bits 5..7) and as an
