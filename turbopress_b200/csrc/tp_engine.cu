@@ -1,23 +1,29 @@
 // Persistent decode engine: a whole chain of packed-TCQ linears in one launch.
 //
-// One CTA per SM stays resident for the program (cooperative launch).  It
-// builds the pair table once.  Each op's weight units (16 rows x 256
-// columns, tile-major, contiguous in the native stream) are split into
-// equal contiguous runs, one per warp of the grid; lane 0 of every warp
-// keeps a ring of `slots` units in flight with bulk copies, walking its
-// runs op after op, so the weights of later layers stream in while an op
-// waits for its activations.  Per op and CTA:
-//   1. wait (bounded) until every CTA finished the op producing x;
-//   2. stage x * rot_scale (fp32) in shared memory in one round of loads,
-//      then transform whole Hadamard blocks (warp registers + shuffles for
-//      blocks <= 1024, CTA-wide above) into fp16 activations in the
-//      decoder's permuted pair order (CTA-wide too for blocks < 32);
+// One CTA per SM stays resident for the program (cooperative launch) and
+// builds the pair table once.  Consecutive ops that read the same input
+// (same x, dependency, width and Hadamard block: q/k/v, gate/up) form a
+// STAGE; a stage is decoded as one matrix whose row tiles are the ops' row
+// tiles one after another (all of them have the same units per row tile).
+// The stage's weight units (16 rows x 256 columns, tile-major, contiguous
+// in each op's native stream) are split into equal contiguous runs, one per
+// warp of the grid; lane 0 of every warp keeps a ring of `slots` units in
+// flight with bulk copies, walking its runs stage after stage, so weights
+// of later layers stream in while a stage waits for its activations.  Per
+// stage and CTA:
+//   1. wait (bounded) until every CTA finished the stage producing x;
+//   2. stage x * rot_scale of every op (fp32) in shared memory in one round
+//      of loads, then transform whole Hadamard blocks (warp registers +
+//      shuffles for blocks 32..1024, CTA-wide otherwise) into fp16
+//      activations in the decoder's permuted pair order, one row per op and
+//      batch row;
 //   3. decode units exactly as the per-call GEMV (level words, pair table,
 //      m16n8k16 MMA), accumulating per row tile in registers, then in
 //      shared memory;
 //   4. scale (and bias, once per row) the CTA's tile partials and add them
-//      to the op's fp32 output with atomics; publish completion.
+//      to the ops' fp32 outputs with atomics; publish completion.
 #include <algorithm>
+#include <vector>
 
 #include "tp_decode.cuh"
 #include "tp_rotate.cuh"
@@ -26,40 +32,52 @@ using namespace tp;
 
 namespace {
 
-constexpr int kEWarps = 8;
+#ifndef TP_EWARPS
+#define TP_EWARPS 8
+#endif
+constexpr int kEWarps = TP_EWARPS;
 constexpr int kEThreads = kEWarps * 32;
 constexpr int kEMaxB = 4;
 constexpr int kEMaxSlots = 16;
-constexpr int kEScratchFloats = 8192;      // largest Hadamard block
-constexpr int kEScratchRowFloats = 12288;  // fp32 activation staging target
+constexpr int kEMaxStageOps = 8;
+constexpr int kEScratchRowFloats = 12288;  // fp32 staging target per pass
+constexpr int kEZStageBytes = 48 * 1024;   // activations of one stage (grouping cap)
 constexpr unsigned kEMaxSpin = 1u << 24;   // dependency polls (~1 s with backoff)
-constexpr int kEMagic = 0x54504531;        // "TPE1"
+constexpr int kEMagic = 0x54504532;        // "TPE2"
 
-struct EOp {
+struct alignas(16) EOp {
   const uint4* stream;
   const uint16_t* scales;
   const uint16_t* bias;
   const uint16_t* rot_scale;
-  const void* x;
   float* y;
-  int32_t x_dtype, dep, n, d;
-  int32_t n_pad, d_pad, units_k, row_tiles;
-  int32_t block, lg, total_units, pad0;
+  int32_t n, tile_base;  // first row tile of this op inside its stage
+  int32_t unit_base, pad0;
   float norm;
   int32_t pad1[3];
 };
 
-struct alignas(16) EHeader {
-  int32_t magic, n_ops, B, bits;
-  int32_t n_states, grid, slots, max_tiles;
-  const uint16_t* codebook;
-  uint32_t ring_off, z_off, scratch_off, red_off;
-  uint32_t smem, d_pad_max, big_blocks, rows_per_pass;
+struct alignas(16) EStage {
+  const void* x;
+  int32_t x_dtype, dep, first_op, n_ops;  // dep: stage index or -1
+  int32_t d, d_pad, units_k, total_tiles;
+  int32_t total_units, vec, block, lg;
+  int32_t rows_per_pass, pad[3];
 };
 
+struct alignas(16) EHeader {
+  int32_t magic, n_ops, n_stages, B;
+  int32_t bits, n_states, grid, slots;
+  const uint16_t* codebook;
+  uint32_t ring_off, z_off, scratch_off, red_off;
+  uint32_t smem, zero_q, max_tiles, pad;
+};
+
+static_assert(sizeof(EOp) % 16 == 0 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
+
 #ifdef TP_TRACE
-// development-only timeline: CTA 0 and CTA gridDim/2 stamp each op's phases
-static __device__ unsigned long long g_etrace[2][512][6];
+// development-only timeline: CTA 0 and CTA gridDim/2 stamp each stage's phases
+static __device__ unsigned long long g_etrace[2][512][8];
 __device__ __forceinline__ void etrace(int o, int k) {
   const int which = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x / 2 ? 1 : -1);
   if (threadIdx.x == 0 && which >= 0 && o < 512) {
@@ -72,9 +90,79 @@ __device__ __forceinline__ void etrace(int o, int k) {
 __device__ __forceinline__ void etrace(int, int) {}
 #endif
 
-__device__ __forceinline__ float load_x(const EOp& op, int64_t i) {
-  if (op.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float*>(op.x) + i);  // produced by this grid
-  return load_as_float(op.x, i, op.x_dtype);
+__device__ __forceinline__ float load_x(const EStage& st, int64_t i) {
+  if (st.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float*>(st.x) + i);  // may be produced by this grid
+  return load_as_float(st.x, i, st.x_dtype);
+}
+
+// Four consecutive x values from flat index 4*q4 (vector path).
+__device__ __forceinline__ float4 load_x4(const EStage& st, int64_t q4) {
+  if (st.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float4*>(st.x) + q4);
+  const uint2 r = __ldcg(reinterpret_cast<const uint2*>(st.x) + q4);
+  if (st.x_dtype == TP_F16) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Jobs are (op j, batch row b) pairs, job = j * B + b.  For jobs
+// [j0, j0 + rows): scratch[(job - j0) * d + c] = x[b][c] * rot_scale_j[c].
+// Every thread issues all of its loads (up to kStageU vectors) before its
+// first use, so a pass costs one L2 round trip instead of one per element.
+constexpr int kStageU = 96 / kEWarps;  // vectors in flight per thread: 12288 floats per CTA
+__device__ __forceinline__ void stage_rows(const EStage& st, const EOp* ops, int B, int j0, int rows, float* scratch,
+                                           int tid) {
+  const int total = rows * st.d;
+  if (st.vec) {
+    const int q4n = total >> 2, dq = st.d >> 2;
+    for (int g0 = tid; g0 < q4n; g0 += kEThreads * kStageU) {
+      float4 xv[kStageU];
+      uint2 rv[kStageU];
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        const int gi = g0 + u * kEThreads;
+        if (gi < q4n) {
+          const int job = j0 + gi / dq, c4 = gi % dq;
+          const int j = job / B, b = job - j * B;
+          rv[u] = __ldg(reinterpret_cast<const uint2*>(ops[st.first_op + j].rot_scale) + c4);
+          xv[u] = load_x4(st, (int64_t)b * dq + c4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        const int gi = g0 + u * kEThreads;
+        if (gi < q4n) {
+          const float2 ra = __half22float2(*reinterpret_cast<const __half2*>(&rv[u].x));
+          const float2 rb = __half22float2(*reinterpret_cast<const __half2*>(&rv[u].y));
+          reinterpret_cast<float4*>(scratch)[gi] =
+              make_float4(xv[u].x * ra.x, xv[u].y * ra.y, xv[u].z * rb.x, xv[u].w * rb.y);
+        }
+      }
+    }
+  } else {
+    for (int g0 = tid; g0 < total; g0 += kEThreads * kStageU) {
+      float xv[kStageU], rv[kStageU];
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        const int gi = g0 + u * kEThreads;
+        if (gi < total) {
+          const int job = j0 + gi / st.d, c = gi % st.d;
+          const int j = job / B, b = job - j * B;
+          rv[u] = h2f_bits(ops[st.first_op + j].rot_scale[c]);
+          xv[u] = load_x(st, (int64_t)b * st.d + c);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        const int gi = g0 + u * kEThreads;
+        if (gi < total) scratch[gi] = xv[u] * rv[u];
+      }
+    }
+  }
 }
 
 // Warp-level FWHT of R*32 elements held as v[r] = element lane + 32 r.
@@ -113,48 +201,81 @@ __device__ __forceinline__ void warp_block_rotate(const float* s, __half* zrow, 
   for (int r = 0; r < R; ++r) zrow[32 * r + zp] = __float2half_rn(v[r] * norm);
 }
 
-// x (all rows, full width) -> fp16 rotated activations in zs.  All threads
-// first stage x * rot_scale for `rows_per_pass` rows in fp32 scratch (one
-// round of independent loads), then warps transform whole blocks from shared
-// memory (blocks <= 1024) or the CTA does (larger blocks).
-__device__ void rotate_op(const EOp& op, int B, int rows_per_pass, __half* zs, float* scratch, int warp, int lane,
-                          int tid) {
+// x -> fp16 rotated activations of every (op, batch row) job of the stage;
+// a job's row lives at zs + job * d_pad.
+__device__ void rotate_stage(const EStage& st, const EOp* ops, int B, __half* zs, float* scratch, int warp, int lane,
+                             int tid, int si) {
   const int zp = zperm_pos(lane);
-  const int nblk = op.d / op.block;
-  for (int b0 = 0; b0 < B; b0 += rows_per_pass) {
-    const int rows = B - b0 < rows_per_pass ? B - b0 : rows_per_pass;
-    for (int rr = 0; rr < rows; ++rr)
-      for (int c = tid; c < op.d; c += kEThreads)
-        scratch[rr * op.d + c] = load_x(op, (int64_t)(b0 + rr) * op.d + c) * h2f_bits(op.rot_scale[c]);
+  const int nblk = st.d / st.block;
+  const int jobs = st.n_ops * B;
+  for (int j0 = 0; j0 < jobs; j0 += st.rows_per_pass) {
+    const int rows = jobs - j0 < st.rows_per_pass ? jobs - j0 : st.rows_per_pass;
+    stage_rows(st, ops, B, j0, rows, scratch, tid);
     __syncthreads();
-    if (op.block >= 32 && op.block <= 1024) {
-      const int R = op.block / 32;
+    if (j0 == 0) etrace(si, 5);
+    if (st.block >= 32 && st.block <= 1024) {
+      const int R = st.block / 32;
       for (int job = warp; job < rows * nblk; job += kEWarps) {
         const int rr = job / nblk, k = job - rr * nblk;
-        const float* s = scratch + rr * op.d + k * op.block;
-        __half* zrow = zs + (size_t)(b0 + rr) * op.d_pad + k * op.block;
+        const float norm = ops[st.first_op + (j0 + rr) / B].norm;
+        const float* s = scratch + rr * st.d + k * st.block;
+        __half* zrow = zs + (size_t)(j0 + rr) * st.d_pad + k * st.block;
         switch (R) {
-          case 1: warp_block_rotate<1>(s, zrow, op.norm, lane, zp); break;
-          case 2: warp_block_rotate<2>(s, zrow, op.norm, lane, zp); break;
-          case 4: warp_block_rotate<4>(s, zrow, op.norm, lane, zp); break;
-          case 8: warp_block_rotate<8>(s, zrow, op.norm, lane, zp); break;
-          case 16: warp_block_rotate<16>(s, zrow, op.norm, lane, zp); break;
-          default: warp_block_rotate<32>(s, zrow, op.norm, lane, zp); break;
+          case 1: warp_block_rotate<1>(s, zrow, norm, lane, zp); break;
+          case 2: warp_block_rotate<2>(s, zrow, norm, lane, zp); break;
+          case 4: warp_block_rotate<4>(s, zrow, norm, lane, zp); break;
+          case 8: warp_block_rotate<8>(s, zrow, norm, lane, zp); break;
+          case 16: warp_block_rotate<16>(s, zrow, norm, lane, zp); break;
+          default: warp_block_rotate<32>(s, zrow, norm, lane, zp); break;
         }
       }
     } else {
-      fwht_shared(scratch, rows * op.d, op.lg);
-      for (int rr = 0; rr < rows; ++rr)
-        for (int c = tid; c < op.d; c += kEThreads)
-          zs[(size_t)(b0 + rr) * op.d_pad + (c & ~31) + zperm_pos(c & 31)] =
-              __float2half_rn(scratch[rr * op.d + c] * op.norm);
+      fwht_shared(scratch, rows * st.d, st.lg);
+      for (int i = tid; i < rows * st.d; i += kEThreads) {
+        const int rr = i / st.d, c = i - rr * st.d;
+        const float norm = ops[st.first_op + (j0 + rr) / B].norm;
+        zs[(size_t)(j0 + rr) * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(scratch[i] * norm);
+      }
     }
     __syncthreads();
   }
-  // padding columns [d, d_pad) of every row
-  for (int b = 0; b < B; ++b)
-    for (int c = op.d + tid; c < op.d_pad; c += kEThreads)
-      zs[(size_t)b * op.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
+  // padding columns [d, d_pad) of every job row
+  if (st.d_pad > st.d)
+    for (int i = tid; i < jobs * (st.d_pad - st.d); i += kEThreads) {
+      const int job = i / (st.d_pad - st.d), c = st.d + i % (st.d_pad - st.d);
+      zs[(size_t)job * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
+    }
+}
+
+// L2 prefetch of what stage `nx` reads with plain loads: every op's
+// rot_scale, scales and bias (spread over the grid's threads, one 128-byte
+// line each), and each warp's trellis-halo unit.  Issued one stage ahead so
+// those loads hit L2 instead of queueing behind the streamed weights.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+__device__ void prefetch_stage(const EStage& nx, const EOp* ops, int64_t v, int64_t V, int lane, int unit_bytes) {
+  const int gt = blockIdx.x * kEThreads + threadIdx.x, nt = gridDim.x * kEThreads;
+  const int rs_lines = (nx.d * 2 + 127) / 128;
+  for (int j = 0; j < nx.n_ops; ++j) {
+    const EOp& op = ops[nx.first_op + j];
+    const int sc_lines = (op.n * 2 + 127) / 128;
+    const int lines = rs_lines + sc_lines * (op.bias ? 2 : 1);
+    for (int l = gt; l < lines; l += nt) {
+      const char* p = l < rs_lines ? reinterpret_cast<const char*>(op.rot_scale) + l * 128
+                    : l < rs_lines + sc_lines ? reinterpret_cast<const char*>(op.scales) + (l - rs_lines) * 128
+                                              : reinterpret_cast<const char*>(op.bias) + (l - rs_lines - sc_lines) * 128;
+      prefetch_l2(p);
+    }
+  }
+  // halo: the unit before this warp's first unit, when that starts inside a row tile
+  const int wb = static_cast<int>(v * nx.total_units / V), we = static_cast<int>((v + 1) * nx.total_units / V);
+  if (wb < we && wb % nx.units_k != 0 && lane * 128 < unit_bytes) {
+    int k = nx.first_op;
+    while (k < nx.first_op + nx.n_ops - 1 && wb - 1 >= ops[k + 1].unit_base) ++k;
+    prefetch_l2(reinterpret_cast<const char*>(ops[k].stream) + (int64_t)(wb - 1 - ops[k].unit_base) * unit_bytes +
+                lane * 128);
+  }
 }
 
 template <int BITS, int S>
@@ -166,6 +287,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
 
   const EHeader hdr = *hdr_g;
   const EOp* ops = reinterpret_cast<const EOp*>(hdr_g + 1);
+  const EStage* stages = reinterpret_cast<const EStage*>(ops + hdr.n_ops);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int G = gridDim.x;
@@ -182,36 +304,49 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const uint32_t cbv = lane < (1 << (BITS + 1)) ? hdr.codebook[lane] : 0u;
   if (tid == 0) s_abort = 0;
 
-  // ---- issue cursor (lane 0): this warp's unit runs, op after op ----
-  int io = 0;
-  int64_t iidx = 0, iend = 0;
+  // ---- issue cursor (lane 0): this warp's unit runs, stage after stage ----
+  int is = 0, ik = 0;    // stage, op
+  int iu = 0, iend = 0;  // stage unit, end of this warp's run
   int n_issued = 0;
-  auto warp_range = [&](int o, int64_t& b, int64_t& e) {
-    const int64_t T = ops[o].total_units;
-    b = v * T / V;
-    e = (v + 1) * T / V;
+  auto warp_range = [&](int s, int& b, int& e) {
+    const int64_t T = stages[s].total_units;
+    b = static_cast<int>(v * T / V);
+    e = static_cast<int>((v + 1) * T / V);
+  };
+  auto seek_op = [&]() {  // ik = op of the current stage that holds unit iu
+    const int last = stages[is].first_op + stages[is].n_ops - 1;
+    while (ik < last && iu >= ops[ik + 1].unit_base) ++ik;
   };
   auto skip_empty = [&]() {
-    while (io < hdr.n_ops && iidx >= iend) {
-      ++io;
-      if (io < hdr.n_ops) warp_range(io, iidx, iend);
+    while (is < hdr.n_stages && iu >= iend) {
+      ++is;
+      if (is < hdr.n_stages) {
+        warp_range(is, iu, iend);
+        ik = stages[is].first_op;
+      }
     }
+    if (is < hdr.n_stages) seek_op();
+  };
+  auto issue = [&](int s) {
+    const EOp& op = ops[ik];
+    bulk_load(ring + (size_t)s * kUnitBytes, op.stream + (int64_t)(iu - op.unit_base) * 32 * BITS, kUnitBytes,
+              &s_bar[warp][s]);
+    ++n_issued;
+    ++iu;
+    if (iu < iend) seek_op();
+    else skip_empty();
   };
   if (lane == 0) {
-    warp_range(0, iidx, iend);
+    warp_range(0, iu, iend);
+    ik = stages[0].first_op;
     skip_empty();
     for (int s = 0; s < slots; ++s) mbar_init(&s_bar[warp][s], 1);
     fence_mbar_init();
-    for (int s = 0; s < slots && io < hdr.n_ops; ++s) {
-      bulk_load(ring + (size_t)s * kUnitBytes, ops[io].stream + iidx * 32 * BITS, kUnitBytes, &s_bar[warp][s]);
-      ++n_issued;
-      ++iidx;
-      skip_empty();
-    }
+    for (int s = 0; s < slots && is < hdr.n_stages; ++s) issue(s);
   }
   build_lut<BITS>(lut, cbv, warp, lane, kEWarps);
   // zero block read by lanes of batch rows >= B
-  if (tid < 16) reinterpret_cast<uint32_t*>(zs + (size_t)B * hdr.d_pad_max)[tid] = 0u;
+  if (tid < 16) reinterpret_cast<uint32_t*>(zs)[hdr.zero_q * 4 + tid] = 0u;
   __syncthreads();
 
   int slot = 0;
@@ -220,14 +355,18 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const uint32_t lanew = BITS <= 3 ? (uint32_t)lane * 4u : (uint32_t)lane * 4u * 0x10001u;
   const int src = (lane & ~3) | ((t + 3) & 3);
 
-  for (int o = 0; o < hdr.n_ops; ++o) {
+  int done_upto = -1;  // newest stage known complete on every CTA (same in all threads)
+  prefetch_stage(stages[0], ops, v, V, lane, kUnitBytes);
+  for (int si = 0; si < hdr.n_stages; ++si) {
     bool ok = true;  // this warp's copies landed
-    const EOp op = ops[o];
-    etrace(o, 0);
-    // ---- 1. dependency ----
-    if (op.dep >= 0) {
+    const EStage st = stages[si];
+    etrace(si, 0);
+    if (si + 1 < hdr.n_stages) prefetch_stage(stages[si + 1], ops, v, V, lane, kUnitBytes);
+    // ---- 1. dependency.  Every CTA publishes its stages in order, so once
+    // stage X is complete on all CTAs every stage before X is too.
+    if (st.dep > done_upto) {
       if (tid == 0) {
-        volatile unsigned* c = counters + op.dep;
+        volatile unsigned* c = counters + st.dep;
         unsigned spins = 0;
         while (*c < (unsigned)G) {
           if (++spins > kEMaxSpin) {
@@ -241,28 +380,33 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       }
       __syncthreads();
       if (s_abort) break;  // CTA-uniform
+      done_upto = st.dep;
     }
-    etrace(o, 1);
+    etrace(si, 1);
     // ---- 2. activations ----
-    rotate_op(op, B, hdr.rows_per_pass, zs, scratch, warp, lane, tid);
-    const int64_t T = op.total_units;
-    const int64_t cb = (int64_t)blockIdx.x * kEWarps * T / V, ce = (int64_t)(blockIdx.x + 1) * kEWarps * T / V;
-    const int t0 = static_cast<int>(cb / op.units_k);
-    const int ntiles = ce > cb ? static_cast<int>((ce - 1) / op.units_k) - t0 + 1 : 0;
+    rotate_stage(st, ops, B, zs, scratch, warp, lane, tid, si);
+    etrace(si, 6);
+    const int T = st.total_units;
+    const int cb = static_cast<int>((int64_t)blockIdx.x * kEWarps * T / V);
+    const int ce = static_cast<int>((int64_t)(blockIdx.x + 1) * kEWarps * T / V);
+    const int t0 = cb / st.units_k;
+    const int ntiles = ce > cb ? (ce - 1) / st.units_k - t0 + 1 : 0;
     for (int i = tid; i < ntiles * kTileRows * Bp; i += kEThreads) red[i] = 0.f;
     __syncthreads();
-    etrace(o, 2);
+    etrace(si, 2);
 
     // ---- 3. decode this warp's units ----
-    int64_t wb, we;
-    warp_range(o, wb, we);
+    int wb, we;
+    warp_range(si, wb, we);
     if (wb < we) {
       float acc[2][1][4];
       int cur_tile = -1;
       uint32_t prevP1g = 0u, prevP1q = 0u;
       const uint4* zq = reinterpret_cast<const uint4*>(zs);
-      const int zrow_stride = op.d_pad / 8;
-      const int zb = g < B ? g * zrow_stride + t * 4 : B * (int)hdr.d_pad_max / 8;
+      const int zrow_q = st.d_pad / 8;  // one job row, in uint4
+      int k = st.first_op;              // op of the current tile
+      const int last_op = st.first_op + st.n_ops - 1;
+      int zb = 0;
       const int zu = g < B ? 1 : 0;
       auto flush = [&](int tile) {
 #pragma unroll
@@ -272,17 +416,20 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
           if (bn < B) atomicAdd(&red[r * Bp + bn], acc[0][0][e] + acc[1][0][e]);
         }
       };
-      int tile = static_cast<int>(wb / op.units_k);
-      int u = static_cast<int>(wb - (int64_t)tile * op.units_k);
-      for (int64_t idx = wb; idx < we; ++idx) {
+      int tile = wb / st.units_k;
+      int u = wb - tile * st.units_k;
+      for (int idx = wb; idx < we; ++idx) {
         if (tile != cur_tile) {
           if (cur_tile >= 0) flush(cur_tile);
           cur_tile = tile;
+          while (k < last_op && tile >= ops[k + 1].tile_base) ++k;
+          zb = g < B ? ((k - st.first_op) * B + g) * zrow_q + t * 4 : static_cast<int>(hdr.zero_q);
 #pragma unroll
           for (int q = 0; q < 2; ++q) acc[q][0][0] = acc[q][0][1] = acc[q][0][2] = acc[q][0][3] = 0.f;
           prevP1g = prevP1q = 0u;
           if (u > 0) {  // trellis halo: last chunk of the previous unit of this row tile
-            const uint4 pv = ldg_stream(op.stream + ((idx - 1) * 32 + lane) * BITS);
+            const EOp& op = ops[k];
+            const uint4 pv = ldg_stream(op.stream + ((int64_t)(idx - 1 - op.unit_base) * 32 + lane) * BITS);
             prevP1g = pv.z;
             prevP1q = pv.w;
           }
@@ -294,15 +441,11 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
         uint4 cur[BITS];
         const uint4* su = reinterpret_cast<const uint4*>(ring + (size_t)slot * kUnitBytes) + lane * BITS;
 #pragma unroll
-        for (int k = 0; k < BITS; ++k) cur[k] = su[k];
+        for (int q = 0; q < BITS; ++q) cur[q] = su[q];
         __syncwarp();
-        if (lane == 0 && io < hdr.n_ops) {  // refill with the next unit of this warp's stream
+        if (lane == 0 && is < hdr.n_stages) {  // refill with the next unit of this warp's runs
           fence_proxy_async();
-          bulk_load(ring + (size_t)slot * kUnitBytes, ops[io].stream + iidx * 32 * BITS, kUnitBytes,
-                    &s_bar[warp][slot]);
-          ++n_issued;
-          ++iidx;
-          skip_empty();
+          issue(slot);
         }
         ++n_consumed;
         if (++slot == slots) {
@@ -337,7 +480,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
           }
           process_chunk<BITS, S, 1>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
         }
-        if (++u == op.units_k) {
+        if (++u == st.units_k) {
           u = 0;
           ++tile;
         }
@@ -349,24 +492,31 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       atomicExch(counters + hdr.n_ops, 2u);
     }
     __syncthreads();
-    etrace(o, 3);
+    etrace(si, 3);
 
     // ---- 4. publish: scaled tile partials into y, bias once per row ----
     for (int i = tid; i < ntiles * kTileRows * B; i += kEThreads) {
       const int bn = i / (ntiles * kTileRows);
       const int rr = i - bn * ntiles * kTileRows;
       const int tile_i = t0 + rr / kTileRows;
-      const int row = tile_i * kTileRows + (rr % kTileRows);
+      int kk = st.first_op;
+      while (kk < st.first_op + st.n_ops - 1 && tile_i >= ops[kk + 1].tile_base) ++kk;
+      const EOp& op = ops[kk];
+      const int row = (tile_i - op.tile_base) * kTileRows + (rr % kTileRows);
       if (row >= op.n) continue;
       float val = red[rr * Bp + bn] * h2f_bits(op.scales[row]);
-      const int64_t first = (int64_t)tile_i * op.units_k;  // unit 0 of this row tile
+      const int first = tile_i * st.units_k;  // unit 0 of this row tile
       if (op.bias && first >= cb && first < ce) val += h2f_bits(op.bias[row]);
       atomicAdd(op.y + (int64_t)bn * op.n + row, val);
     }
-    __threadfence();
+    // CTA barrier, then one gpu-scope fence (cumulative over the writes the
+    // barrier ordered before it) ahead of the completion count
     __syncthreads();
-    if (tid == 0) atomicAdd(counters + o, 1u);
-    etrace(o, 4);
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(counters + si, 1u);
+    }
+    etrace(si, 4);
     if (s_abort) break;  // read after the barrier above: CTA-uniform
   }
 
@@ -429,7 +579,7 @@ tp_status launch_engine_s(const EHeader& h, const void* img, unsigned* c, cudaSt
 
 extern "C" int64_t tp_engine_image_bytes(int n_ops) {
   if (n_ops < 1) return -1;
-  return (int64_t)sizeof(EHeader) + (int64_t)n_ops * (int64_t)sizeof(EOp);
+  return (int64_t)sizeof(EHeader) + (int64_t)n_ops * (int64_t)(sizeof(EOp) + sizeof(EStage));
 }
 
 extern "C" int64_t tp_engine_counter_bytes(int n_ops) {
@@ -445,12 +595,8 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   if (B < 1 || B > kEMaxB) return fail(TP_ERR_UNSUPPORTED, "engine: batch must be 1..%d (got %d)", kEMaxB, B);
   if (bits < 1 || bits > 4) return fail(TP_ERR_UNSUPPORTED, "engine: bits must be 1..4 (got %d)", bits);
   if (log2_states(n_states) < 0) return fail(TP_ERR_UNSUPPORTED, "n_states must be 4, 8, 16 or 64");
-  EHeader* h = static_cast<EHeader*>(image);
-  EOp* eo = reinterpret_cast<EOp*>(h + 1);
   const int G = sm_count_e();
   const int64_t V = (int64_t)G * kEWarps;
-  int64_t d_pad_max = 0, max_tiles = 1;
-  bool big = false;
   for (int i = 0; i < n_ops; ++i) {
     const tp_engine_op& s = ops[i];
     if (!s.tcq_stream || !s.scales || !s.rot_scale || !s.x || !s.y || s.n < 1 || s.d < 1)
@@ -460,60 +606,100 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
     if (s.dep >= i || s.dep < -1) return fail(TP_ERR_ARG, "engine op %d: dep must be -1 or an earlier op", i);
     if (s.dep >= 0 && (s.x_dtype != TP_F32 || ops[s.dep].n != s.d || s.x != ops[s.dep].y))
       return fail(TP_ERR_ARG, "engine op %d: a dependent input must be op %d's fp32 output", i, s.dep);
-    if (s.block < 1 || s.block > kEScratchFloats || (s.block & (s.block - 1)) || s.d % s.block)
+    if (s.block < 1 || s.block > 8192 || (s.block & (s.block - 1)) || s.d % s.block)
       return fail(TP_ERR_UNSUPPORTED, "engine op %d: Hadamard block %d unsupported (1..8192)", i, s.block);
-    if (s.n > (int64_t)1 << 30 || s.d > (int64_t)1 << 20) return fail(TP_ERR_UNSUPPORTED, "engine op %d too big", i);
-    EOp e{};
-    e.stream = reinterpret_cast<const uint4*>(s.tcq_stream);
-    e.scales = s.scales;
-    e.bias = s.bias;
-    e.rot_scale = s.rot_scale;
-    e.x = s.x;
-    e.y = s.y;
-    e.x_dtype = s.x_dtype;
-    e.dep = s.dep;
-    e.n = static_cast<int32_t>(s.n);
-    e.d = static_cast<int32_t>(s.d);
-    e.n_pad = static_cast<int32_t>(pad_to(s.n, kTileRows));
-    e.d_pad = static_cast<int32_t>(pad_to(s.d, kUnitCols));
-    e.units_k = e.d_pad / kUnitCols;
-    e.row_tiles = e.n_pad / kTileRows;
-    e.block = s.block;
-    int lg = 0;
-    while ((1 << lg) < s.block) ++lg;
-    e.lg = lg;
-    e.total_units = e.row_tiles * e.units_k;
-    e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(s.block)));
-    eo[i] = e;
-    d_pad_max = std::max<int64_t>(d_pad_max, e.d_pad);
-    const int64_t per_cta = (kEWarps * (int64_t)e.total_units + V - 1) / V;
-    max_tiles = std::max<int64_t>(max_tiles, per_cta / e.units_k + 2);
-    big = big || s.block > 1024;
+    if (s.n > (int64_t)1 << 26 || s.d > (int64_t)1 << 20) return fail(TP_ERR_UNSUPPORTED, "engine op %d too big", i);
+  }
+  // ---- group consecutive ops with the same input into stages ----
+  std::vector<EStage> st;
+  std::vector<int> stage_of(n_ops);
+  for (int i = 0; i < n_ops; ++i) {
+    const tp_engine_op& s = ops[i];
+    const int64_t d_pad = pad_to(s.d, kUnitCols);
+    bool join = false;
+    if (!st.empty()) {
+      const EStage& c = st.back();
+      const tp_engine_op& f = ops[c.first_op];
+      join = f.x == s.x && f.x_dtype == s.x_dtype && f.dep == s.dep && f.d == s.d && f.block == s.block &&
+             c.n_ops < kEMaxStageOps && (int64_t)(c.n_ops + 1) * B * d_pad * 2 <= kEZStageBytes;
+    }
+    if (!join) {
+      EStage e{};
+      e.x = s.x;
+      e.x_dtype = s.x_dtype;
+      e.dep = s.dep < 0 ? -1 : stage_of[s.dep];
+      e.first_op = i;
+      e.d = static_cast<int32_t>(s.d);
+      e.d_pad = static_cast<int32_t>(d_pad);
+      e.units_k = e.d_pad / kUnitCols;
+      e.block = s.block;
+      int lg = 0;
+      while ((1 << lg) < s.block) ++lg;
+      e.lg = lg;
+      const uintptr_t xa = s.x_dtype == TP_F32 ? 16 : 8;
+      e.vec = (s.d % 4 == 0 && aligned(s.x, xa)) ? 1 : 0;
+      st.push_back(e);
+    }
+    stage_of[i] = static_cast<int>(st.size()) - 1;
+    EStage& c = st.back();
+    c.n_ops += 1;
+    if (!aligned(s.rot_scale, 8)) c.vec = 0;
+  }
+  const int n_stages = static_cast<int>(st.size());
+  EHeader* h = static_cast<EHeader*>(image);
+  EOp* eo = reinterpret_cast<EOp*>(h + 1);
+  EStage* es = reinterpret_cast<EStage*>(eo + n_ops);
+  int64_t max_tiles = 1, zrows_q = 0, scratch_floats = 0;
+  for (int si = 0; si < n_stages; ++si) {
+    EStage& c = st[si];
+    int64_t tiles = 0;
+    for (int i = c.first_op; i < c.first_op + c.n_ops; ++i) {
+      EOp e{};
+      e.stream = reinterpret_cast<const uint4*>(ops[i].tcq_stream);
+      e.scales = ops[i].scales;
+      e.bias = ops[i].bias;
+      e.rot_scale = ops[i].rot_scale;
+      e.y = ops[i].y;
+      e.n = static_cast<int32_t>(ops[i].n);
+      e.tile_base = static_cast<int32_t>(tiles);
+      e.unit_base = static_cast<int32_t>(tiles * c.units_k);
+      e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(ops[i].block)));
+      eo[i] = e;
+      tiles += pad_to(ops[i].n, kTileRows) / kTileRows;
+    }
+    if (tiles * c.units_k > (int64_t)1 << 30) return fail(TP_ERR_UNSUPPORTED, "engine: stage %d too big", si);
+    c.total_tiles = static_cast<int32_t>(tiles);
+    c.total_units = static_cast<int32_t>(tiles * c.units_k);
+    const int64_t jobs = (int64_t)c.n_ops * B;
+    c.rows_per_pass =
+        static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(jobs, kEScratchRowFloats / c.d_pad)));
+    scratch_floats = std::max<int64_t>(scratch_floats, (int64_t)c.rows_per_pass * c.d_pad);
+    zrows_q = std::max<int64_t>(zrows_q, jobs * c.d_pad / 8);
+    const int64_t per_cta = (kEWarps * (int64_t)c.total_units + V - 1) / V;
+    max_tiles = std::max<int64_t>(max_tiles, per_cta / c.units_k + 2);
+    es[si] = c;
   }
   EHeader hh{};
   hh.magic = kEMagic;
   hh.n_ops = n_ops;
+  hh.n_stages = n_stages;
   hh.B = B;
   hh.bits = bits;
   hh.n_states = n_states;
   hh.grid = G;
-  hh.max_tiles = static_cast<int32_t>(max_tiles);
   hh.codebook = codebook;
-  hh.d_pad_max = static_cast<uint32_t>(d_pad_max);
-  hh.big_blocks = big ? 1u : 0u;
+  hh.max_tiles = static_cast<uint32_t>(max_tiles);
+  hh.zero_q = static_cast<uint32_t>(zrows_q);  // 64 zero bytes after the widest stage's rows
   const uint32_t lut = bits == 4 ? LutCfg<4>::kLutBytes : LutCfg<3>::kLutBytes;
-  const uint64_t zbytes = (uint64_t)B * d_pad_max * 2 + 64;
-  // fp32 staging of x * rot_scale: whole rows, as many as fit kEScratchRowFloats
-  const int64_t rpp = std::max<int64_t>(1, std::min<int64_t>(B, kEScratchRowFloats / d_pad_max));
-  hh.rows_per_pass = static_cast<uint32_t>(rpp);
-  const uint64_t scratch = (uint64_t)std::max<int64_t>(rpp * d_pad_max, big ? kEScratchFloats : 0) * 4;
+  const uint64_t zbytes = (uint64_t)zrows_q * 16 + 64;
+  const uint64_t scratch = (uint64_t)scratch_floats * 4;
   const uint64_t red = (uint64_t)max_tiles * kTileRows * 8 * 4;
   const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red);
   const uint64_t budget = 227u * 1024u - 2048u;
   const uint64_t unit = 512u * bits;
   if (fixed + kEWarps * 2 * unit > budget)
-    return fail(TP_ERR_UNSUPPORTED, "engine: activations (d=%lld, B=%d) do not fit shared memory",
-                (long long)d_pad_max, B);
+    return fail(TP_ERR_UNSUPPORTED, "engine: activations (%lld halves, B=%d) do not fit shared memory",
+                (long long)(zrows_q * 8), B);
   hh.slots = static_cast<int32_t>(std::min<uint64_t>(kEMaxSlots, (budget - fixed) / (kEWarps * unit)));
   hh.ring_off = lut;
   hh.z_off = al128(hh.ring_off + (uint64_t)kEWarps * hh.slots * unit);

@@ -132,14 +132,17 @@ class DecodeEngine:
         if x is not None:
             for t in ([x] if isinstance(x, Tensor) else x):
                 self.set_input(t)
-        lib = _abi.lib()
         with torch.cuda.device(self.device):
             self.y_arena.zero_()
             self.counters.zero_()
-            st = torch.cuda.current_stream(self.device).cuda_stream
-            _abi.check(lib.tp_engine_run(self.image.data_ptr(), self._image_host.ctypes.data,
-                                         self.counters.data_ptr(), st), "engine_run")
+            self.launch()
         return self.outputs
+
+    def launch(self) -> None:
+        """The engine kernel alone (outputs and counters must be zero)."""
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        _abi.check(_abi.lib().tp_engine_run(self.image.data_ptr(), self._image_host.ctypes.data,
+                                            self.counters.data_ptr(), st), "engine_run")
 
     def check(self) -> None:
         """Raise if the last run gave up (a dependency or copy wait timed out)."""
