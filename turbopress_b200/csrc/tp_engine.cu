@@ -33,7 +33,7 @@ using namespace tp;
 namespace {
 
 #ifndef TP_EWARPS
-#define TP_EWARPS 8
+#define TP_EWARPS 12
 #endif
 constexpr int kEWarps = TP_EWARPS;
 constexpr int kEThreads = kEWarps * 32;
@@ -44,6 +44,7 @@ constexpr int kEScratchRowFloats = 12288;  // fp32 staging target per pass
 constexpr int kEZStageBytes = 48 * 1024;   // activations of one stage (grouping cap)
 constexpr unsigned kEMaxSpin = 1u << 24;   // dependency polls (~1 s with backoff)
 constexpr int kEMagic = 0x54504532;        // "TPE2"
+constexpr unsigned kEStaticSmem = 4096;    // bound on the kernel's static shared memory
 
 struct alignas(16) EOp {
   const uint4* stream;
@@ -53,8 +54,6 @@ struct alignas(16) EOp {
   float* y;
   int32_t n, tile_base;  // first row tile of this op inside its stage
   int32_t unit_base, pad0;
-  float norm;
-  int32_t pad1[3];
 };
 
 struct alignas(16) EStage {
@@ -62,7 +61,9 @@ struct alignas(16) EStage {
   int32_t x_dtype, dep, first_op, n_ops;  // dep: stage index or -1
   int32_t d, d_pad, units_k, total_tiles;
   int32_t total_units, vec, block, lg;
-  int32_t rows_per_pass, pad[3];
+  int32_t rows_per_pass;
+  float norm;  // 1/sqrt(block)
+  int32_t pad[2];
 };
 
 struct alignas(16) EHeader {
@@ -70,9 +71,10 @@ struct alignas(16) EHeader {
   int32_t bits, n_states, grid, slots;
   const uint16_t* codebook;
   uint32_t ring_off, z_off, scratch_off, red_off;
-  uint32_t smem, zero_q, max_tiles, pad;
+  uint32_t smem, zero_q, max_tiles, sc_off;  // sc_off: per-CTA row scales, then biases (fp16)
 };
 
+static_assert(sizeof(EOp) == 64 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
 static_assert(sizeof(EOp) % 16 == 0 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
 
 #ifdef TP_TRACE
@@ -95,6 +97,16 @@ __device__ __forceinline__ float load_x(const EStage& st, int64_t i) {
   return load_as_float(st.x, i, st.x_dtype);
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// copies src_bytes (0..4) and zero-fills the rest of the 4 bytes
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Four consecutive x values from flat index 4*q4 (vector path).
 __device__ __forceinline__ float4 load_x4(const EStage& st, int64_t q4) {
   if (st.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float4*>(st.x) + q4);
@@ -114,8 +126,8 @@ __device__ __forceinline__ float4 load_x4(const EStage& st, int64_t q4) {
 // Every thread issues all of its loads (up to kStageU vectors) before its
 // first use, so a pass costs one L2 round trip instead of one per element.
 constexpr int kStageU = 96 / kEWarps;  // vectors in flight per thread: 12288 floats per CTA
-__device__ __forceinline__ void stage_rows(const EStage& st, const EOp* ops, int B, int j0, int rows, float* scratch,
-                                           int tid) {
+__device__ __forceinline__ void stage_rows(const EStage& st, const EOp* cops, int B, int j0, int rows,
+                                           float* scratch, int tid) {
   const int total = rows * st.d;
   if (st.vec) {
     const int q4n = total >> 2, dq = st.d >> 2;
@@ -128,7 +140,7 @@ __device__ __forceinline__ void stage_rows(const EStage& st, const EOp* ops, int
         if (gi < q4n) {
           const int job = j0 + gi / dq, c4 = gi % dq;
           const int j = job / B, b = job - j * B;
-          rv[u] = __ldg(reinterpret_cast<const uint2*>(ops[st.first_op + j].rot_scale) + c4);
+          rv[u] = __ldg(reinterpret_cast<const uint2*>(cops[j].rot_scale) + c4);
           xv[u] = load_x4(st, (int64_t)b * dq + c4);
         }
       }
@@ -152,7 +164,7 @@ __device__ __forceinline__ void stage_rows(const EStage& st, const EOp* ops, int
         if (gi < total) {
           const int job = j0 + gi / st.d, c = gi % st.d;
           const int j = job / B, b = job - j * B;
-          rv[u] = h2f_bits(ops[st.first_op + j].rot_scale[c]);
+          rv[u] = h2f_bits(cops[j].rot_scale[c]);
           xv[u] = load_x(st, (int64_t)b * st.d + c);
         }
       }
@@ -202,49 +214,49 @@ __device__ __forceinline__ void warp_block_rotate(const float* s, __half* zrow, 
 }
 
 // x -> fp16 rotated activations of every (op, batch row) job of the stage;
-// a job's row lives at zs + job * d_pad.
-__device__ void rotate_stage(const EStage& st, const EOp* ops, int B, __half* zs, float* scratch, int warp, int lane,
-                             int tid, int si) {
+// a job's row lives at zs + job * d_pad.  Ends with a CTA barrier.
+__device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* zs, float* scratch, int warp,
+                             int lane, int tid, int si) {
   const int zp = zperm_pos(lane);
   const int nblk = st.d / st.block;
   const int jobs = st.n_ops * B;
+  const int npad = st.d_pad - st.d;
   for (int j0 = 0; j0 < jobs; j0 += st.rows_per_pass) {
     const int rows = jobs - j0 < st.rows_per_pass ? jobs - j0 : st.rows_per_pass;
-    stage_rows(st, ops, B, j0, rows, scratch, tid);
+    stage_rows(st, cops, B, j0, rows, scratch, tid);
     __syncthreads();
     if (j0 == 0) etrace(si, 5);
     if (st.block >= 32 && st.block <= 1024) {
       const int R = st.block / 32;
       for (int job = warp; job < rows * nblk; job += kEWarps) {
         const int rr = job / nblk, k = job - rr * nblk;
-        const float norm = ops[st.first_op + (j0 + rr) / B].norm;
         const float* s = scratch + rr * st.d + k * st.block;
         __half* zrow = zs + (size_t)(j0 + rr) * st.d_pad + k * st.block;
         switch (R) {
-          case 1: warp_block_rotate<1>(s, zrow, norm, lane, zp); break;
-          case 2: warp_block_rotate<2>(s, zrow, norm, lane, zp); break;
-          case 4: warp_block_rotate<4>(s, zrow, norm, lane, zp); break;
-          case 8: warp_block_rotate<8>(s, zrow, norm, lane, zp); break;
-          case 16: warp_block_rotate<16>(s, zrow, norm, lane, zp); break;
-          default: warp_block_rotate<32>(s, zrow, norm, lane, zp); break;
+          case 1: warp_block_rotate<1>(s, zrow, st.norm, lane, zp); break;
+          case 2: warp_block_rotate<2>(s, zrow, st.norm, lane, zp); break;
+          case 4: warp_block_rotate<4>(s, zrow, st.norm, lane, zp); break;
+          case 8: warp_block_rotate<8>(s, zrow, st.norm, lane, zp); break;
+          case 16: warp_block_rotate<16>(s, zrow, st.norm, lane, zp); break;
+          default: warp_block_rotate<32>(s, zrow, st.norm, lane, zp); break;
         }
       }
     } else {
       fwht_shared(scratch, rows * st.d, st.lg);
-      for (int i = tid; i < rows * st.d; i += kEThreads) {
-        const int rr = i / st.d, c = i - rr * st.d;
-        const float norm = ops[st.first_op + (j0 + rr) / B].norm;
-        zs[(size_t)(j0 + rr) * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(scratch[i] * norm);
+      for (int rr = 0; rr < rows; ++rr) {
+        const float* srow = scratch + rr * st.d;
+        __half* zrow = zs + (size_t)(j0 + rr) * st.d_pad;
+        for (int c = tid; c < st.d; c += kEThreads)
+          zrow[(c & ~31) + zperm_pos(c & 31)] = __float2half_rn(srow[c] * st.norm);
       }
+    }
+    // padding columns [d, d_pad) of this pass's rows
+    for (int i = tid; i < rows * npad; i += kEThreads) {
+      const int rr = i / npad, c = st.d + (i - rr * npad);
+      zs[(size_t)(j0 + rr) * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
     }
     __syncthreads();
   }
-  // padding columns [d, d_pad) of every job row
-  if (st.d_pad > st.d)
-    for (int i = tid; i < jobs * (st.d_pad - st.d); i += kEThreads) {
-      const int job = i / (st.d_pad - st.d), c = st.d + i % (st.d_pad - st.d);
-      zs[(size_t)job * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
-    }
 }
 
 // L2 prefetch of what stage `nx` reads with plain loads: every op's
@@ -254,11 +266,11 @@ __device__ void rotate_stage(const EStage& st, const EOp* ops, int B, __half* zs
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
-__device__ void prefetch_stage(const EStage& nx, const EOp* ops, int64_t v, int64_t V, int lane, int unit_bytes) {
+__device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int64_t V, int lane, int unit_bytes) {
   const int gt = blockIdx.x * kEThreads + threadIdx.x, nt = gridDim.x * kEThreads;
   const int rs_lines = (nx.d * 2 + 127) / 128;
   for (int j = 0; j < nx.n_ops; ++j) {
-    const EOp& op = ops[nx.first_op + j];
+    const EOp& op = nops[j];
     const int sc_lines = (op.n * 2 + 127) / 128;
     const int lines = rs_lines + sc_lines * (op.bias ? 2 : 1);
     for (int l = gt; l < lines; l += nt) {
@@ -271,9 +283,9 @@ __device__ void prefetch_stage(const EStage& nx, const EOp* ops, int64_t v, int6
   // halo: the unit before this warp's first unit, when that starts inside a row tile
   const int wb = static_cast<int>(v * nx.total_units / V), we = static_cast<int>((v + 1) * nx.total_units / V);
   if (wb < we && wb % nx.units_k != 0 && lane * 128 < unit_bytes) {
-    int k = nx.first_op;
-    while (k < nx.first_op + nx.n_ops - 1 && wb - 1 >= ops[k + 1].unit_base) ++k;
-    prefetch_l2(reinterpret_cast<const char*>(ops[k].stream) + (int64_t)(wb - 1 - ops[k].unit_base) * unit_bytes +
+    int k = 0;
+    while (k < nx.n_ops - 1 && wb - 1 >= nops[k + 1].unit_base) ++k;
+    prefetch_l2(reinterpret_cast<const char*>(nops[k].stream) + (int64_t)(wb - 1 - nops[k].unit_base) * unit_bytes +
                 lane * 128);
   }
 }
@@ -283,6 +295,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
                                                                   unsigned* __restrict__ counters) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t s_bar[kEWarps][kEMaxSlots];
+  __shared__ __align__(16) EOp s_ops[3][kEMaxStageOps];  // descriptors of stages si, si+1, si+2
+  __shared__ __align__(16) EStage s_st[3];
   __shared__ int s_abort;
 
   const EHeader hdr = *hdr_g;
@@ -299,7 +313,23 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   __half* zs = reinterpret_cast<__half*>(smem + hdr.z_off);
   float* scratch = reinterpret_cast<float*>(smem + hdr.scratch_off);
   float* red = reinterpret_cast<float*>(smem + hdr.red_off);
+  uint16_t* s_sc = reinterpret_cast<uint16_t*>(smem + hdr.sc_off);  // [max_tiles * 16]
+  uint16_t* s_bi = s_sc + hdr.max_tiles * kTileRows;
   const int slots = hdr.slots;
+
+  // descriptor cache: stage s (and up to kEMaxStageOps ops from op f) ->
+  // buffer s % 3 with async copies; complete at the issuing threads' next
+  // cp_async_wait_all
+  auto load_desc = [&](int s, int f) {
+    constexpr int kStChunks = sizeof(EStage) / 16, kOpChunks = sizeof(EOp) / 16;
+    const int cnt = min(kEMaxStageOps, hdr.n_ops - f);
+    const int b = s % 3;
+    if (tid < kStChunks)
+      cp_async16(reinterpret_cast<char*>(&s_st[b]) + tid * 16, reinterpret_cast<const char*>(stages + s) + tid * 16);
+    else if (tid < kStChunks + cnt * kOpChunks)
+      cp_async16(reinterpret_cast<char*>(&s_ops[b][0]) + (tid - kStChunks) * 16,
+                 reinterpret_cast<const char*>(ops + f) + (tid - kStChunks) * 16);
+  };
 
   const uint32_t cbv = lane < (1 << (BITS + 1)) ? hdr.codebook[lane] : 0u;
   if (tid == 0) s_abort = 0;
@@ -344,9 +374,15 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     fence_mbar_init();
     for (int s = 0; s < slots && is < hdr.n_stages; ++s) issue(s);
   }
+  load_desc(0, 0);
   build_lut<BITS>(lut, cbv, warp, lane, kEWarps);
-  // zero block read by lanes of batch rows >= B
+  // zero block read by lanes of batch rows >= B; tile partials start at zero
   if (tid < 16) reinterpret_cast<uint32_t*>(zs)[hdr.zero_q * 4 + tid] = 0u;
+  for (int i = tid; i < (int)hdr.max_tiles * kTileRows * 8; i += kEThreads) red[i] = 0.f;
+  cp_async_wait_all();
+  __syncthreads();
+  if (hdr.n_stages > 1) load_desc(1, s_st[0].first_op + s_st[0].n_ops);
+  cp_async_wait_all();
   __syncthreads();
 
   int slot = 0;
@@ -356,12 +392,33 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const int src = (lane & ~3) | ((t + 3) & 3);
 
   int done_upto = -1;  // newest stage known complete on every CTA (same in all threads)
-  prefetch_stage(stages[0], ops, v, V, lane, kUnitBytes);
-  for (int si = 0; si < hdr.n_stages; ++si) {
+  prefetch_stage(s_st[0], s_ops[0], v, V, lane, kUnitBytes);
+  for (int si = 0, buf = 0; si < hdr.n_stages; ++si, buf = buf == 2 ? 0 : buf + 1) {
     bool ok = true;  // this warp's copies landed
-    const EStage st = stages[si];
+    const EStage st = s_st[buf];
+    const EOp* cops = s_ops[buf];
+    const int nbuf = buf == 2 ? 0 : buf + 1;
     etrace(si, 0);
-    if (si + 1 < hdr.n_stages) prefetch_stage(stages[si + 1], ops, v, V, lane, kUnitBytes);
+    if (si + 2 < hdr.n_stages) load_desc(si + 2, s_st[nbuf].first_op + s_st[nbuf].n_ops);
+    if (si + 1 < hdr.n_stages) prefetch_stage(s_st[nbuf], s_ops[nbuf], v, V, lane, kUnitBytes);
+    const int T = st.total_units;
+    const int cb = static_cast<int>((int64_t)blockIdx.x * kEWarps * T / V);
+    const int ce = static_cast<int>((int64_t)(blockIdx.x + 1) * kEWarps * T / V);
+    const int t0 = cb / st.units_k;
+    const int ntiles = ce > cb ? (ce - 1) / st.units_k - t0 + 1 : 0;
+    // this CTA's row scales and biases (2 rows per 4-byte copy, zero past n)
+    for (int i = tid; i < ntiles * 16; i += kEThreads) {
+      const int tl = i >> 4, pr = (i >> 1) & 7, which = i & 1;
+      const int tile_i = t0 + tl;
+      int j = 0;
+      while (j < st.n_ops - 1 && tile_i >= cops[j + 1].tile_base) ++j;
+      const int row = (tile_i - cops[j].tile_base) * kTileRows + 2 * pr;
+      const int nb = max(0, min(4, (cops[j].n - row) * 2));
+      const uint16_t* base = which ? cops[j].bias : cops[j].scales;
+      uint16_t* dst = (which ? s_bi : s_sc) + tl * kTileRows + 2 * pr;
+      if (base) cp_async4(dst, base + (nb ? row : 0), nb);
+      else cp_async4(dst, cops[j].scales, 0);
+    }
     // ---- 1. dependency.  Every CTA publishes its stages in order, so once
     // stage X is complete on all CTAs every stage before X is too.
     if (st.dep > done_upto) {
@@ -384,15 +441,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     }
     etrace(si, 1);
     // ---- 2. activations ----
-    rotate_stage(st, ops, B, zs, scratch, warp, lane, tid, si);
+    rotate_stage(st, cops, B, zs, scratch, warp, lane, tid, si);
     etrace(si, 6);
-    const int T = st.total_units;
-    const int cb = static_cast<int>((int64_t)blockIdx.x * kEWarps * T / V);
-    const int ce = static_cast<int>((int64_t)(blockIdx.x + 1) * kEWarps * T / V);
-    const int t0 = cb / st.units_k;
-    const int ntiles = ce > cb ? (ce - 1) / st.units_k - t0 + 1 : 0;
-    for (int i = tid; i < ntiles * kTileRows * Bp; i += kEThreads) red[i] = 0.f;
-    __syncthreads();
     etrace(si, 2);
 
     // ---- 3. decode this warp's units ----
@@ -404,8 +454,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       uint32_t prevP1g = 0u, prevP1q = 0u;
       const uint4* zq = reinterpret_cast<const uint4*>(zs);
       const int zrow_q = st.d_pad / 8;  // one job row, in uint4
-      int k = st.first_op;              // op of the current tile
-      const int last_op = st.first_op + st.n_ops - 1;
+      int k = 0;                        // op (within the stage) of the current tile
+      const int last_op = st.n_ops - 1;
       int zb = 0;
       const int zu = g < B ? 1 : 0;
       auto flush = [&](int tile) {
@@ -422,13 +472,13 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
         if (tile != cur_tile) {
           if (cur_tile >= 0) flush(cur_tile);
           cur_tile = tile;
-          while (k < last_op && tile >= ops[k + 1].tile_base) ++k;
-          zb = g < B ? ((k - st.first_op) * B + g) * zrow_q + t * 4 : static_cast<int>(hdr.zero_q);
+          while (k < last_op && tile >= cops[k + 1].tile_base) ++k;
+          zb = g < B ? (k * B + g) * zrow_q + t * 4 : static_cast<int>(hdr.zero_q);
 #pragma unroll
           for (int q = 0; q < 2; ++q) acc[q][0][0] = acc[q][0][1] = acc[q][0][2] = acc[q][0][3] = 0.f;
           prevP1g = prevP1q = 0u;
           if (u > 0) {  // trellis halo: last chunk of the previous unit of this row tile
-            const EOp& op = ops[k];
+            const EOp& op = cops[k];
             const uint4 pv = ldg_stream(op.stream + ((int64_t)(idx - 1 - op.unit_base) * 32 + lane) * BITS);
             prevP1g = pv.z;
             prevP1q = pv.w;
@@ -491,6 +541,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       s_abort = 1;
       atomicExch(counters + hdr.n_ops, 2u);
     }
+    cp_async_wait_all();  // row scales / biases and the descriptors of stage si + 2
     __syncthreads();
     etrace(si, 3);
 
@@ -499,14 +550,16 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       const int bn = i / (ntiles * kTileRows);
       const int rr = i - bn * ntiles * kTileRows;
       const int tile_i = t0 + rr / kTileRows;
-      int kk = st.first_op;
-      while (kk < st.first_op + st.n_ops - 1 && tile_i >= ops[kk + 1].tile_base) ++kk;
-      const EOp& op = ops[kk];
+      int kk = 0;
+      while (kk < st.n_ops - 1 && tile_i >= cops[kk + 1].tile_base) ++kk;
+      const EOp& op = cops[kk];
       const int row = (tile_i - op.tile_base) * kTileRows + (rr % kTileRows);
+      const float part = red[rr * Bp + bn];
+      red[rr * Bp + bn] = 0.f;  // ready for the next stage
       if (row >= op.n) continue;
-      float val = red[rr * Bp + bn] * h2f_bits(op.scales[row]);
-      const int first = tile_i * st.units_k;  // unit 0 of this row tile
-      if (op.bias && first >= cb && first < ce) val += h2f_bits(op.bias[row]);
+      float val = part * h2f_bits(s_sc[rr]);
+      const int first = tile_i * st.units_k;  // unit 0 of this row tile: its CTA adds the bias
+      if (first >= cb && first < ce) val += h2f_bits(s_bi[rr]);
       atomicAdd(op.y + (int64_t)bn * op.n + row, val);
     }
     // CTA barrier, then one gpu-scope fence (cumulative over the writes the
@@ -520,6 +573,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     if (s_abort) break;  // read after the barrier above: CTA-uniform
   }
 
+  cp_async_wait_all();
   // ---- drain copies still in flight (only after an abort) ----
   if (lane == 0) {
     while (n_consumed < n_issued) {
@@ -547,6 +601,11 @@ tp_status launch_engine_t(const EHeader& h, const void* image_dev, unsigned* cou
   auto kern = tcq_engine_kernel<BITS, S>;
   static int smem_set[64] = {0};
   if (tp_status s = ensure_smem(kern, h.smem, smem_set, "cudaFuncSetAttribute(engine)")) return s;
+  cudaFuncAttributes fa{};
+  TP_CUDA_TRY(cudaFuncGetAttributes(&fa, kern), "engine attributes");
+  if (fa.sharedSizeBytes > kEStaticSmem)
+    return fail(TP_ERR_UNSUPPORTED, "engine: static shared memory %zu above the %u reserved", fa.sharedSizeBytes,
+                kEStaticSmem);
   int occ = 0;
   TP_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kEThreads, h.smem), "engine occupancy");
   if (occ < 1) return fail(TP_ERR_UNSUPPORTED, "engine: one CTA per SM does not fit (smem %u)", h.smem);
@@ -602,6 +661,8 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
     if (!s.tcq_stream || !s.scales || !s.rot_scale || !s.x || !s.y || s.n < 1 || s.d < 1)
       return fail(TP_ERR_ARG, "engine op %d: bad arguments", i);
     if (!aligned(s.tcq_stream, 16)) return fail(TP_ERR_ALIGN, "engine op %d: stream must be 16-byte aligned", i);
+    if (!aligned(s.scales, 4) || (s.bias && !aligned(s.bias, 4)))
+      return fail(TP_ERR_ALIGN, "engine op %d: scales and bias must be 4-byte aligned", i);
     if (!valid_dtype(s.x_dtype)) return fail(TP_ERR_ARG, "engine op %d: bad x dtype", i);
     if (s.dep >= i || s.dep < -1) return fail(TP_ERR_ARG, "engine op %d: dep must be -1 or an earlier op", i);
     if (s.dep >= 0 && (s.x_dtype != TP_F32 || ops[s.dep].n != s.d || s.x != ops[s.dep].y))
@@ -636,6 +697,7 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
       int lg = 0;
       while ((1 << lg) < s.block) ++lg;
       e.lg = lg;
+      e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(s.block)));
       const uintptr_t xa = s.x_dtype == TP_F32 ? 16 : 8;
       e.vec = (s.d % 4 == 0 && aligned(s.x, xa)) ? 1 : 0;
       st.push_back(e);
@@ -663,7 +725,6 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
       e.n = static_cast<int32_t>(ops[i].n);
       e.tile_base = static_cast<int32_t>(tiles);
       e.unit_base = static_cast<int32_t>(tiles * c.units_k);
-      e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(ops[i].block)));
       eo[i] = e;
       tiles += pad_to(ops[i].n, kTileRows) / kTileRows;
     }
@@ -694,8 +755,9 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   const uint64_t zbytes = (uint64_t)zrows_q * 16 + 64;
   const uint64_t scratch = (uint64_t)scratch_floats * 4;
   const uint64_t red = (uint64_t)max_tiles * kTileRows * 8 * 4;
-  const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red);
-  const uint64_t budget = 227u * 1024u - 2048u;
+  const uint64_t rowc = (uint64_t)max_tiles * kTileRows * 2 * 2;  // row scales + biases
+  const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red) + al128(rowc);
+  const uint64_t budget = 227u * 1024u - kEStaticSmem;
   const uint64_t unit = 512u * bits;
   if (fixed + kEWarps * 2 * unit > budget)
     return fail(TP_ERR_UNSUPPORTED, "engine: activations (%lld halves, B=%d) do not fit shared memory",
@@ -705,7 +767,8 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   hh.z_off = al128(hh.ring_off + (uint64_t)kEWarps * hh.slots * unit);
   hh.scratch_off = al128(hh.z_off + zbytes);
   hh.red_off = al128(hh.scratch_off + scratch);
-  hh.smem = al128(hh.red_off + red);
+  hh.sc_off = al128(hh.red_off + red);
+  hh.smem = al128(hh.sc_off + rowc);
   *h = hh;
   return clear_ok();
 }
