@@ -62,6 +62,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// one arrival on `bar`
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// non-blocking: true when the phase with `parity` has completed
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
 // true when the phase with `parity` completed; false after kMaxPolls polls
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   const uint32_t a = smem_u32(bar);

@@ -7,19 +7,24 @@
 // tiles one after another (all of them have the same units per row tile).
 // The stage's weight units (16 rows x 256 columns, tile-major, contiguous
 // in each op's native stream) are split into equal contiguous runs, one per
-// warp of the grid; lane 0 of every warp keeps a ring of `slots` units in
-// flight with bulk copies, walking its runs stage after stage, so weights
-// of later layers stream in while a stage waits for its activations.  Per
-// stage and CTA:
+// consumer warp of the grid.
+//
+// Warp roles inside a CTA: kEWarps consumer warps decode; one producer warp
+// keeps, for every consumer, a ring of `slots` units in flight with bulk
+// copies (lane w serves consumer w: full barrier per slot completed by the
+// copy, empty barrier per slot released by the consumer), walking the
+// consumer's runs stage after stage, so weights of later layers stream in
+// while a stage waits for its input.  Per stage the consumers (synchronised
+// among themselves with a named barrier; the producer never joins it):
 //   1. wait (bounded) until every CTA finished the stage producing x;
 //   2. stage x * rot_scale of every op (fp32) in shared memory in one round
 //      of loads, then transform whole Hadamard blocks (warp registers +
-//      shuffles for blocks 32..1024, CTA-wide otherwise) into fp16
+//      shuffles for blocks 32..1024, consumer-wide otherwise) into fp16
 //      activations in the decoder's permuted pair order, one row per op and
 //      batch row;
-//   3. decode units exactly as the per-call GEMV (level words, pair table,
-//      m16n8k16 MMA), accumulating per row tile in registers, then in
-//      shared memory;
+//   3. decode units as the per-call GEMV (level words, pair table, m16n8k16
+//      MMA), two units per iteration where the run allows, accumulating per
+//      row tile in registers, then in shared memory;
 //   4. scale (and bias, once per row) the CTA's tile partials and add them
 //      to the ops' fp32 outputs with atomics; publish completion.
 #include <algorithm>
@@ -33,17 +38,22 @@ using namespace tp;
 namespace {
 
 #ifndef TP_EWARPS
-#define TP_EWARPS 12
+#define TP_EWARPS 11
 #endif
-constexpr int kEWarps = TP_EWARPS;
-constexpr int kEThreads = kEWarps * 32;
+constexpr int kEWarps = TP_EWARPS;             // consumer warps
+constexpr int kECThreads = kEWarps * 32;       // consumer threads
+constexpr int kEThreads = kECThreads + 32;     // + the producer warp
 constexpr int kEMaxB = 4;
-constexpr int kEMaxSlots = 16;
+#ifndef TP_EMAXSLOTS
+#define TP_EMAXSLOTS 8
+#endif
+constexpr int kEMaxSlots = TP_EMAXSLOTS;
 constexpr int kEMaxStageOps = 8;
-constexpr int kEScratchRowFloats = 12288;  // fp32 staging target per pass
+constexpr int kEXStageBytes = 48 * 1024;   // staged x rows per pass
 constexpr int kEZStageBytes = 48 * 1024;   // activations of one stage (grouping cap)
 constexpr unsigned kEMaxSpin = 1u << 24;   // dependency polls (~1 s with backoff)
-constexpr int kEMagic = 0x54504532;        // "TPE2"
+constexpr unsigned kEMaxIdle = 1u << 25;   // producer polls without progress (~4 s)
+constexpr int kEMagic = 0x54504533;        // "TPE3"
 constexpr unsigned kEStaticSmem = 4096;    // bound on the kernel's static shared memory
 
 struct alignas(16) EOp {
@@ -61,9 +71,9 @@ struct alignas(16) EStage {
   int32_t x_dtype, dep, first_op, n_ops;  // dep: stage index or -1
   int32_t d, d_pad, units_k, total_tiles;
   int32_t total_units, vec, block, lg;
-  int32_t rows_per_pass;
-  float norm;  // 1/sqrt(block)
-  int32_t pad[2];
+  int32_t rows_per_pass;       // batch rows of x staged per pass
+  float norm;                  // 1/sqrt(block)
+  uint32_t rs_off, work_off;   // in the scratch area: staged rot_scale rows, fp32 work row
 };
 
 struct alignas(16) EHeader {
@@ -75,7 +85,6 @@ struct alignas(16) EHeader {
 };
 
 static_assert(sizeof(EOp) == 64 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
-static_assert(sizeof(EOp) % 16 == 0 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
 
 #ifdef TP_TRACE
 // development-only timeline: CTA 0 and CTA gridDim/2 stamp each stage's phases
@@ -92,9 +101,22 @@ __device__ __forceinline__ void etrace(int o, int k) {
 __device__ __forceinline__ void etrace(int, int) {}
 #endif
 
+// barrier of the consumer warps only (the producer warp runs its own loop)
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kECThreads) : "memory"); }
+
 __device__ __forceinline__ float load_x(const EStage& st, int64_t i) {
   if (st.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float*>(st.x) + i);  // may be produced by this grid
   return load_as_float(st.x, i, st.x_dtype);
+}
+
+// completion counters: release increment / acquire read at gpu scope
+__device__ __forceinline__ void red_release(unsigned* p) {
+  asm volatile("fence.acq_rel.gpu;\n red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -107,74 +129,42 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Four consecutive x values from flat index 4*q4 (vector path).
-__device__ __forceinline__ float4 load_x4(const EStage& st, int64_t q4) {
-  if (st.x_dtype == TP_F32) return __ldcg(reinterpret_cast<const float4*>(st.x) + q4);
-  const uint2 r = __ldcg(reinterpret_cast<const uint2*>(st.x) + q4);
-  if (st.x_dtype == TP_F16) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
-    return make_float4(a.x, a.y, b.x, b.y);
+// Stage the inputs of a rotation pass in the scratch area: x rows
+// [b0, b0 + rows) at offset 0 and, on the first pass, every op's rot_scale
+// row at rs_off.  Aligned stages copy raw bytes with cp.async (all copies in
+// flight at once: one round trip whatever the size); others convert x to
+// fp32 with plain loads.
+__device__ void stage_inputs(const EStage& st, const EOp* cops, int b0, int rows, bool first, unsigned char* scr,
+                             int ctid) {
+  if (st.vec) {
+    const int esz = st.x_dtype == TP_F32 ? 4 : 2;
+    const int rowc = st.d * esz / 16;
+    const char* xsrc = reinterpret_cast<const char*>(st.x) + (size_t)b0 * st.d * esz;
+    for (int i = ctid; i < rows * rowc; i += kECThreads) cp_async16(scr + i * 16, xsrc + i * 16);
+    if (first) {
+      const int rc = st.d * 2 / 16;
+      for (int j = 0; j < st.n_ops; ++j)
+        for (int i = ctid; i < rc; i += kECThreads)
+          cp_async16(scr + st.rs_off + j * st.d * 2 + i * 16, reinterpret_cast<const char*>(cops[j].rot_scale) + i * 16);
+    }
+    cp_async_wait_all();
+  } else {
+    float* xs = reinterpret_cast<float*>(scr);
+    for (int r = 0; r < rows; ++r)
+      for (int c = ctid; c < st.d; c += kECThreads) xs[r * st.d + c] = load_x(st, (int64_t)(b0 + r) * st.d + c);
+    if (first) {
+      uint16_t* rs = reinterpret_cast<uint16_t*>(scr + st.rs_off);
+      for (int j = 0; j < st.n_ops; ++j)
+        for (int c = ctid; c < st.d; c += kECThreads) rs[j * st.d + c] = cops[j].rot_scale[c];
+    }
   }
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
-  return make_float4(a.x, a.y, b.x, b.y);
 }
 
-// Jobs are (op j, batch row b) pairs, job = j * B + b.  For jobs
-// [j0, j0 + rows): scratch[(job - j0) * d + c] = x[b][c] * rot_scale_j[c].
-// Every thread issues all of its loads (up to kStageU vectors) before its
-// first use, so a pass costs one L2 round trip instead of one per element.
-constexpr int kStageU = 96 / kEWarps;  // vectors in flight per thread: 12288 floats per CTA
-__device__ __forceinline__ void stage_rows(const EStage& st, const EOp* cops, int B, int j0, int rows,
-                                           float* scratch, int tid) {
-  const int total = rows * st.d;
-  if (st.vec) {
-    const int q4n = total >> 2, dq = st.d >> 2;
-    for (int g0 = tid; g0 < q4n; g0 += kEThreads * kStageU) {
-      float4 xv[kStageU];
-      uint2 rv[kStageU];
-#pragma unroll
-      for (int u = 0; u < kStageU; ++u) {
-        const int gi = g0 + u * kEThreads;
-        if (gi < q4n) {
-          const int job = j0 + gi / dq, c4 = gi % dq;
-          const int j = job / B, b = job - j * B;
-          rv[u] = __ldg(reinterpret_cast<const uint2*>(cops[j].rot_scale) + c4);
-          xv[u] = load_x4(st, (int64_t)b * dq + c4);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kStageU; ++u) {
-        const int gi = g0 + u * kEThreads;
-        if (gi < q4n) {
-          const float2 ra = __half22float2(*reinterpret_cast<const __half2*>(&rv[u].x));
-          const float2 rb = __half22float2(*reinterpret_cast<const __half2*>(&rv[u].y));
-          reinterpret_cast<float4*>(scratch)[gi] =
-              make_float4(xv[u].x * ra.x, xv[u].y * ra.y, xv[u].z * rb.x, xv[u].w * rb.y);
-        }
-      }
-    }
-  } else {
-    for (int g0 = tid; g0 < total; g0 += kEThreads * kStageU) {
-      float xv[kStageU], rv[kStageU];
-#pragma unroll
-      for (int u = 0; u < kStageU; ++u) {
-        const int gi = g0 + u * kEThreads;
-        if (gi < total) {
-          const int job = j0 + gi / st.d, c = gi % st.d;
-          const int j = job / B, b = job - j * B;
-          rv[u] = h2f_bits(cops[j].rot_scale[c]);
-          xv[u] = load_x(st, (int64_t)b * st.d + c);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kStageU; ++u) {
-        const int gi = g0 + u * kEThreads;
-        if (gi < total) scratch[gi] = xv[u] * rv[u];
-      }
-    }
-  }
+// element i of the staged x rows
+__device__ __forceinline__ float xs_at(const unsigned char* scr, int dt, int i) {
+  if (dt == TP_F32) return reinterpret_cast<const float*>(scr)[i];
+  if (dt == TP_F16) return __half2float(reinterpret_cast<const __half*>(scr)[i]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(scr)[i]);
 }
 
 // Warp-level FWHT of R*32 elements held as v[r] = element lane + 32 r.
@@ -193,81 +183,159 @@ __device__ __forceinline__ void warp_fwht_regs(float* v, int lane) {
   }
 #pragma unroll
   for (int m = 1; m < 32; m <<= 1) {
-    const bool upper = lane & m;
+    const float sgn = (lane & m) ? -1.f : 1.f;  // upper lane: o - v, lower lane: o + v
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const float o = __shfl_xor_sync(0xffffffffu, v[r], m);
-      v[r] = upper ? o - v[r] : v[r] + o;
+      v[r] = fmaf(sgn, v[r], o);
     }
   }
 }
 
-// one Hadamard block (32R columns of fp32 x*rot_scale at `s`) -> zs row
+// one Hadamard block: x (staged, dtype dt, from element xoff) * rot_scale
+// row -> FWHT -> fp16 zs row in the decoder's permuted order
 template <int R>
-__device__ __forceinline__ void warp_block_rotate(const float* s, __half* zrow, float norm, int lane, int zp) {
+__device__ __forceinline__ void warp_block_rotate(const unsigned char* scr, int dt, int xoff, const uint16_t* rs,
+                                                  __half* zrow, float norm, int lane, int zp) {
   float v[R];
 #pragma unroll
-  for (int r = 0; r < R; ++r) v[r] = s[lane + 32 * r];
+  for (int r = 0; r < R; ++r) v[r] = xs_at(scr, dt, xoff + lane + 32 * r) * h2f_bits(rs[lane + 32 * r]);
   warp_fwht_regs<R>(v, lane);
 #pragma unroll
   for (int r = 0; r < R; ++r) zrow[32 * r + zp] = __float2half_rn(v[r] * norm);
 }
 
-// x -> fp16 rotated activations of every (op, batch row) job of the stage;
-// a job's row lives at zs + job * d_pad.  Ends with a CTA barrier.
-__device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* zs, float* scratch, int warp,
-                             int lane, int tid, int si) {
+// Butterflies over index bits [b_start, lg) of s[0, count) by the consumer
+// threads (radix-8 groups, one consumer barrier per group of three bits).
+__device__ void fwht_consumers(float* s, int count, int b_start, int lg, int ctid) {
+  for (int b0 = b_start; b0 < lg; b0 += 3) {
+    const int nb = lg - b0 < 3 ? lg - b0 : 3;
+    const int G = 1 << nb;
+    const int groups = count >> nb;
+    for (int grp = ctid; grp < groups; grp += kECThreads) {
+      const int lo = grp & ((1 << b0) - 1);
+      const int hi = grp >> b0;
+      const int base = (hi << (b0 + nb)) | lo;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < G) v[e] = s[base + (e << b0)];
+#pragma unroll
+      for (int h = 1; h < 8; h <<= 1) {
+        if (h >= G) break;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e < G && !(e & h)) {
+            const float a = v[e], b = v[e + h];
+            v[e] = a + b;
+            v[e + h] = a - b;
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < G) s[base + (e << b0)] = v[e];
+    }
+    csync();
+  }
+}
+
+// x -> fp16 rotated activations of every (op j, batch row b) job of the
+// stage; the job's row lives at zs + (j * B + b) * d_pad.  Blocks of
+// 32..1024 are one warp job each (registers + shuffles); larger blocks go
+// through the fp32 work row as 512-wide warp transforms plus consumer-wide
+// passes over the upper index bits, smaller ones consumer-wide.  Ends with a
+// consumer barrier.
+__device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* zs, unsigned char* scr, int warp,
+                             int lane, int ctid, int si) {
   const int zp = zperm_pos(lane);
   const int nblk = st.d / st.block;
-  const int jobs = st.n_ops * B;
-  const int npad = st.d_pad - st.d;
-  for (int j0 = 0; j0 < jobs; j0 += st.rows_per_pass) {
-    const int rows = jobs - j0 < st.rows_per_pass ? jobs - j0 : st.rows_per_pass;
-    stage_rows(st, cops, B, j0, rows, scratch, tid);
-    __syncthreads();
-    if (j0 == 0) etrace(si, 5);
+  const int dt = st.vec ? st.x_dtype : TP_F32;
+  const uint16_t* rs = reinterpret_cast<const uint16_t*>(scr + st.rs_off);
+  for (int b0 = 0; b0 < B; b0 += st.rows_per_pass) {
+    const int rows = B - b0 < st.rows_per_pass ? B - b0 : st.rows_per_pass;
+    stage_inputs(st, cops, b0, rows, b0 == 0, scr, ctid);
+    csync();
+    if (b0 == 0) etrace(si, 5);
     if (st.block >= 32 && st.block <= 1024) {
+      // warp jobs (op j, row rr, block kb), kb fastest
       const int R = st.block / 32;
-      for (int job = warp; job < rows * nblk; job += kEWarps) {
-        const int rr = job / nblk, k = job - rr * nblk;
-        const float* s = scratch + rr * st.d + k * st.block;
-        __half* zrow = zs + (size_t)(j0 + rr) * st.d_pad + k * st.block;
+      int j = 0, rr = 0, kb = warp;
+      while (kb >= nblk) {
+        kb -= nblk;
+        if (++rr == rows) {
+          rr = 0;
+          ++j;
+        }
+      }
+      while (j < st.n_ops) {
+        const int xoff = rr * st.d + kb * st.block;
+        const uint16_t* rsb = rs + j * st.d + kb * st.block;
+        __half* zrow = zs + (size_t)(j * B + b0 + rr) * st.d_pad + kb * st.block;
         switch (R) {
-          case 1: warp_block_rotate<1>(s, zrow, st.norm, lane, zp); break;
-          case 2: warp_block_rotate<2>(s, zrow, st.norm, lane, zp); break;
-          case 4: warp_block_rotate<4>(s, zrow, st.norm, lane, zp); break;
-          case 8: warp_block_rotate<8>(s, zrow, st.norm, lane, zp); break;
-          case 16: warp_block_rotate<16>(s, zrow, st.norm, lane, zp); break;
-          default: warp_block_rotate<32>(s, zrow, st.norm, lane, zp); break;
+          case 1: warp_block_rotate<1>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+          case 2: warp_block_rotate<2>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+          case 4: warp_block_rotate<4>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+          case 8: warp_block_rotate<8>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+          case 16: warp_block_rotate<16>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+          default: warp_block_rotate<32>(scr, dt, xoff, rsb, zrow, st.norm, lane, zp); break;
+        }
+        kb += kEWarps;
+        while (kb >= nblk) {
+          kb -= nblk;
+          if (++rr == rows) {
+            rr = 0;
+            ++j;
+          }
         }
       }
     } else {
-      fwht_shared(scratch, rows * st.d, st.lg);
-      for (int rr = 0; rr < rows; ++rr) {
-        const float* srow = scratch + rr * st.d;
-        __half* zrow = zs + (size_t)(j0 + rr) * st.d_pad;
-        for (int c = tid; c < st.d; c += kEThreads)
-          zrow[(c & ~31) + zperm_pos(c & 31)] = __float2half_rn(srow[c] * st.norm);
-      }
+      // one job at a time through the fp32 work row
+      float* work = reinterpret_cast<float*>(scr + st.work_off);
+      for (int j = 0; j < st.n_ops; ++j)
+        for (int rr = 0; rr < rows; ++rr) {
+          for (int c = ctid; c < st.d; c += kECThreads)
+            work[c] = xs_at(scr, dt, rr * st.d + c) * h2f_bits(rs[j * st.d + c]);
+          csync();
+          int b_start = 0;
+          if (st.block > 1024) {
+            for (int sb = warp; sb < st.d / 512; sb += kEWarps) {
+              float v[16];
+#pragma unroll
+              for (int r = 0; r < 16; ++r) v[r] = work[sb * 512 + lane + 32 * r];
+              warp_fwht_regs<16>(v, lane);
+#pragma unroll
+              for (int r = 0; r < 16; ++r) work[sb * 512 + lane + 32 * r] = v[r];
+            }
+            csync();
+            b_start = 9;
+          }
+          fwht_consumers(work, st.d, b_start, st.lg, ctid);
+          __half* zrow = zs + (size_t)(j * B + b0 + rr) * st.d_pad;
+          for (int c = ctid; c < st.d; c += kECThreads)
+            zrow[(c & ~31) + zperm_pos(c & 31)] = __float2half_rn(work[c] * st.norm);
+          csync();
+        }
     }
-    // padding columns [d, d_pad) of this pass's rows
-    for (int i = tid; i < rows * npad; i += kEThreads) {
-      const int rr = i / npad, c = st.d + (i - rr * npad);
-      zs[(size_t)(j0 + rr) * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
-    }
-    __syncthreads();
+    csync();
+  }
+  // padding columns [d, d_pad) of every job row
+  if (st.d_pad > st.d) {
+    for (int jr = 0; jr < st.n_ops * B; ++jr)
+      for (int c = st.d + ctid; c < st.d_pad; c += kECThreads)
+        zs[(size_t)jr * st.d_pad + (c & ~31) + zperm_pos(c & 31)] = __float2half_rn(0.f);
+    csync();
   }
 }
 
 // L2 prefetch of what stage `nx` reads with plain loads: every op's
-// rot_scale, scales and bias (spread over the grid's threads, one 128-byte
-// line each), and each warp's trellis-halo unit.  Issued one stage ahead so
-// those loads hit L2 instead of queueing behind the streamed weights.
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-__device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int64_t V, int lane, int unit_bytes) {
-  const int gt = blockIdx.x * kEThreads + threadIdx.x, nt = gridDim.x * kEThreads;
+// rot_scale, scales and bias (spread over the grid's consumer threads, one
+// 128-byte line each), and each warp's trellis-halo unit.  Issued one stage
+// ahead so those loads hit L2 instead of queueing behind the streamed weights.
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+__device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int64_t V, int lane, int ctid,
+                               int unit_bytes) {
+  const int gt = blockIdx.x * kECThreads + ctid, nt = gridDim.x * kECThreads;
   const int rs_lines = (nx.d * 2 + 127) / 128;
   for (int j = 0; j < nx.n_ops; ++j) {
     const EOp& op = nops[j];
@@ -275,8 +343,9 @@ __device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int
     const int lines = rs_lines + sc_lines * (op.bias ? 2 : 1);
     for (int l = gt; l < lines; l += nt) {
       const char* p = l < rs_lines ? reinterpret_cast<const char*>(op.rot_scale) + l * 128
-                    : l < rs_lines + sc_lines ? reinterpret_cast<const char*>(op.scales) + (l - rs_lines) * 128
-                                              : reinterpret_cast<const char*>(op.bias) + (l - rs_lines - sc_lines) * 128;
+                      : l < rs_lines + sc_lines
+                          ? reinterpret_cast<const char*>(op.scales) + (l - rs_lines) * 128
+                          : reinterpret_cast<const char*>(op.bias) + (l - rs_lines - sc_lines) * 128;
       prefetch_l2(p);
     }
   }
@@ -290,11 +359,48 @@ __device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int
   }
 }
 
+// One unit (two 32-column chunks per lane) into `acc`; `prevg/prevq` carry
+// the trellis halo (last path words of the previous unit of the row tile).
+template <int BITS, int S>
+__device__ __forceinline__ void decode_unit(const unsigned char* lut, uint32_t lanew, const uint4* zq,
+                                            const uint4 (&cur)[BITS], uint32_t& prevg, uint32_t& prevq, int t,
+                                            int src, int zoff0, int zstep, float (*acc)[1][4]) {
+  const uint32_t P0g = cur[0].x, P0q = cur[0].y, P1g = cur[0].z, P1q = cur[0].w;
+  const uint32_t H0g = __shfl_sync(0xffffffffu, t == 3 ? prevg : P0g, src);
+  const uint32_t H0q = __shfl_sync(0xffffffffu, t == 3 ? prevq : P0q, src);
+  const uint32_t H1g = __shfl_sync(0xffffffffu, t == 3 ? P0g : P1g, src);
+  const uint32_t H1q = __shfl_sync(0xffffffffu, t == 3 ? P0q : P1q, src);
+  prevg = P1g;
+  prevq = P1q;
+#pragma unroll
+  for (int cgi = 0; cgi < 2; ++cgi) {
+    int zoff[1];
+    zoff[0] = zoff0 + cgi * zstep;
+    const uint32_t Pg = cgi ? P1g : P0g, Pq = cgi ? P1q : P0q;
+    const uint32_t Hg = cgi ? H1g : H0g, Hq = cgi ? H1q : H0q;
+    uint32_t Mg0 = 0u, Mq0 = 0u, Mg1 = 0u, Mq1 = 0u, Mg2 = 0u, Mq2 = 0u;
+    if (BITS >= 2) {
+      Mg0 = cgi ? cur[1].z : cur[1].x;
+      Mq0 = cgi ? cur[1].w : cur[1].y;
+    }
+    if (BITS >= 3) {
+      Mg1 = cgi ? cur[2].z : cur[2].x;
+      Mq1 = cgi ? cur[2].w : cur[2].y;
+    }
+    if (BITS >= 4) {
+      Mg2 = cgi ? cur[3].z : cur[3].x;
+      Mq2 = cgi ? cur[3].w : cur[3].y;
+    }
+    process_chunk<BITS, S, 1>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
+  }
+}
+
 template <int BITS, int S>
 __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader* __restrict__ hdr_g,
                                                                   unsigned* __restrict__ counters) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t s_bar[kEWarps][kEMaxSlots];
+  __shared__ __align__(8) uint64_t s_full[kEWarps][kEMaxSlots];
+  __shared__ __align__(8) uint64_t s_empty[kEWarps][kEMaxSlots];
   __shared__ __align__(16) EOp s_ops[3][kEMaxStageOps];  // descriptors of stages si, si+1, si+2
   __shared__ __align__(16) EStage s_st[3];
   __shared__ int s_abort;
@@ -305,21 +411,20 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int G = gridDim.x;
-  const int64_t V = (int64_t)G * kEWarps, v = (int64_t)blockIdx.x * kEWarps + warp;
+  const int64_t V = (int64_t)G * kEWarps;
   const int B = hdr.B, Bp = 8;
   constexpr unsigned kUnitBytes = 32u * 16u * BITS;
   unsigned char* lut = smem;
-  unsigned char* ring = smem + hdr.ring_off + (size_t)warp * hdr.slots * kUnitBytes;
   __half* zs = reinterpret_cast<__half*>(smem + hdr.z_off);
-  float* scratch = reinterpret_cast<float*>(smem + hdr.scratch_off);
+  unsigned char* scratch = smem + hdr.scratch_off;
   float* red = reinterpret_cast<float*>(smem + hdr.red_off);
   uint16_t* s_sc = reinterpret_cast<uint16_t*>(smem + hdr.sc_off);  // [max_tiles * 16]
   uint16_t* s_bi = s_sc + hdr.max_tiles * kTileRows;
   const int slots = hdr.slots;
 
   // descriptor cache: stage s (and up to kEMaxStageOps ops from op f) ->
-  // buffer s % 3 with async copies; complete at the issuing threads' next
-  // cp_async_wait_all
+  // buffer s % 3 with async copies by consumer threads; complete at the
+  // issuing threads' next cp_async_wait_all
   auto load_desc = [&](int s, int f) {
     constexpr int kStChunks = sizeof(EStage) / 16, kOpChunks = sizeof(EOp) / 16;
     const int cnt = min(kEMaxStageOps, hdr.n_ops - f);
@@ -333,66 +438,99 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
 
   const uint32_t cbv = lane < (1 << (BITS + 1)) ? hdr.codebook[lane] : 0u;
   if (tid == 0) s_abort = 0;
-
-  // ---- issue cursor (lane 0): this warp's unit runs, stage after stage ----
-  int is = 0, ik = 0;    // stage, op
-  int iu = 0, iend = 0;  // stage unit, end of this warp's run
-  int n_issued = 0;
-  auto warp_range = [&](int s, int& b, int& e) {
-    const int64_t T = stages[s].total_units;
-    b = static_cast<int>(v * T / V);
-    e = static_cast<int>((v + 1) * T / V);
-  };
-  auto seek_op = [&]() {  // ik = op of the current stage that holds unit iu
-    const int last = stages[is].first_op + stages[is].n_ops - 1;
-    while (ik < last && iu >= ops[ik + 1].unit_base) ++ik;
-  };
-  auto skip_empty = [&]() {
-    while (is < hdr.n_stages && iu >= iend) {
-      ++is;
-      if (is < hdr.n_stages) {
-        warp_range(is, iu, iend);
-        ik = stages[is].first_op;
-      }
-    }
-    if (is < hdr.n_stages) seek_op();
-  };
-  auto issue = [&](int s) {
-    const EOp& op = ops[ik];
-    bulk_load(ring + (size_t)s * kUnitBytes, op.stream + (int64_t)(iu - op.unit_base) * 32 * BITS, kUnitBytes,
-              &s_bar[warp][s]);
-    ++n_issued;
-    ++iu;
-    if (iu < iend) seek_op();
-    else skip_empty();
-  };
-  if (lane == 0) {
-    warp_range(0, iu, iend);
-    ik = stages[0].first_op;
-    skip_empty();
-    for (int s = 0; s < slots; ++s) mbar_init(&s_bar[warp][s], 1);
-    fence_mbar_init();
-    for (int s = 0; s < slots && is < hdr.n_stages; ++s) issue(s);
+  if (tid < kEWarps * kEMaxSlots) {
+    mbar_init(&s_full[0][0] + tid, 1);
+    mbar_init(&s_empty[0][0] + tid, 1);
   }
-  load_desc(0, 0);
-  build_lut<BITS>(lut, cbv, warp, lane, kEWarps);
+  fence_mbar_init();
+  if (tid < kECThreads) load_desc(0, 0);
+  build_lut<BITS>(lut, cbv, warp, lane, kEWarps + 1);
   // zero block read by lanes of batch rows >= B; tile partials start at zero
   if (tid < 16) reinterpret_cast<uint32_t*>(zs)[hdr.zero_q * 4 + tid] = 0u;
   for (int i = tid; i < (int)hdr.max_tiles * kTileRows * 8; i += kEThreads) red[i] = 0.f;
   cp_async_wait_all();
   __syncthreads();
-  if (hdr.n_stages > 1) load_desc(1, s_st[0].first_op + s_st[0].n_ops);
+  if (tid < kECThreads && hdr.n_stages > 1) load_desc(1, s_st[0].first_op + s_st[0].n_ops);
   cp_async_wait_all();
   __syncthreads();
 
+  // ===================== producer warp =====================
+  if (warp == kEWarps) {
+    const int w = lane;  // consumer served by this lane
+    const int64_t v = (int64_t)blockIdx.x * kEWarps + w;
+    unsigned char* ring = smem + hdr.ring_off + (size_t)w * slots * kUnitBytes;
+    int is = 0, ik = 0, iu = 0, iend = 0, slot = 0, n_iss = 0;
+    unsigned eph = 0;
+    auto warp_range = [&](int s) {
+      const int64_t T = stages[s].total_units;
+      iu = static_cast<int>(v * T / V);
+      iend = static_cast<int>((v + 1) * T / V);
+      ik = stages[s].first_op;
+    };
+    auto seek = [&]() {  // next non-empty run, and the op holding unit iu
+      while (is < hdr.n_stages && iu >= iend) {
+        ++is;
+        if (is < hdr.n_stages) warp_range(is);
+      }
+      if (is < hdr.n_stages) {
+        const int last = stages[is].first_op + stages[is].n_ops - 1;
+        while (ik < last && iu >= ops[ik + 1].unit_base) ++ik;
+      }
+    };
+    bool active = w < kEWarps;
+    if (active) {
+      warp_range(0);
+      seek();
+      active = is < hdr.n_stages;
+    }
+    unsigned idle = 0;
+    while (__any_sync(0xffffffffu, active)) {
+      bool did = false;
+      if (active && mbar_test(&s_empty[w][slot], eph ^ 1u)) {
+        const EOp& op = ops[ik];
+        bulk_load(ring + (size_t)slot * kUnitBytes, op.stream + (int64_t)(iu - op.unit_base) * 32 * BITS,
+                  kUnitBytes, &s_full[w][slot]);
+        ++n_iss;
+        if (++slot == slots) {
+          slot = 0;
+          eph ^= 1u;
+        }
+        ++iu;
+        seek();
+        active = is < hdr.n_stages;
+        did = true;
+      }
+      if (__any_sync(0xffffffffu, did)) {
+        idle = 0;
+      } else {
+        if (*reinterpret_cast<volatile int*>(&s_abort) || ++idle > kEMaxIdle) break;
+        __nanosleep(128);
+      }
+    }
+    // every issued copy must land before the CTA exits: wait (bounded) for
+    // the phase of the last copy issued into each slot
+    if (w < kEWarps) {
+      const int last = min(n_iss, slots);
+      for (int k = 0; k < last; ++k) {
+        const int i = n_iss - 1 - k;  // issue index
+        const int s = i % slots;
+        mbar_wait(&s_full[w][s], (unsigned)((i / slots) & 1));
+      }
+    }
+    return;
+  }
+
+  // ===================== consumer warps =====================
+  const int ctid = tid;
+  const int64_t v = (int64_t)blockIdx.x * kEWarps + warp;
+  const unsigned char* ring = smem + hdr.ring_off + (size_t)warp * slots * kUnitBytes;
   int slot = 0;
-  unsigned parity = 0u;
-  int n_consumed = 0;
+  unsigned fph = 0u;
   const uint32_t lanew = BITS <= 3 ? (uint32_t)lane * 4u : (uint32_t)lane * 4u * 0x10001u;
   const int src = (lane & ~3) | ((t + 3) & 3);
 
-  int done_upto = -1;  // newest stage known complete on every CTA (same in all threads)
-  prefetch_stage(s_st[0], s_ops[0], v, V, lane, kUnitBytes);
+  int done_upto = -1;  // newest stage known complete on every CTA (same in all consumer threads)
+  prefetch_stage(s_st[0], s_ops[0], v, V, lane, ctid, kUnitBytes);
   for (int si = 0, buf = 0; si < hdr.n_stages; ++si, buf = buf == 2 ? 0 : buf + 1) {
     bool ok = true;  // this warp's copies landed
     const EStage st = s_st[buf];
@@ -400,14 +538,14 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     const int nbuf = buf == 2 ? 0 : buf + 1;
     etrace(si, 0);
     if (si + 2 < hdr.n_stages) load_desc(si + 2, s_st[nbuf].first_op + s_st[nbuf].n_ops);
-    if (si + 1 < hdr.n_stages) prefetch_stage(s_st[nbuf], s_ops[nbuf], v, V, lane, kUnitBytes);
+    if (si + 1 < hdr.n_stages) prefetch_stage(s_st[nbuf], s_ops[nbuf], v, V, lane, ctid, kUnitBytes);
     const int T = st.total_units;
     const int cb = static_cast<int>((int64_t)blockIdx.x * kEWarps * T / V);
     const int ce = static_cast<int>((int64_t)(blockIdx.x + 1) * kEWarps * T / V);
     const int t0 = cb / st.units_k;
     const int ntiles = ce > cb ? (ce - 1) / st.units_k - t0 + 1 : 0;
     // this CTA's row scales and biases (2 rows per 4-byte copy, zero past n)
-    for (int i = tid; i < ntiles * 16; i += kEThreads) {
+    for (int i = ctid; i < ntiles * 16; i += kECThreads) {
       const int tl = i >> 4, pr = (i >> 1) & 7, which = i & 1;
       const int tile_i = t0 + tl;
       int j = 0;
@@ -422,10 +560,9 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     // ---- 1. dependency.  Every CTA publishes its stages in order, so once
     // stage X is complete on all CTAs every stage before X is too.
     if (st.dep > done_upto) {
-      if (tid == 0) {
-        volatile unsigned* c = counters + st.dep;
+      if (ctid == 0) {
         unsigned spins = 0;
-        while (*c < (unsigned)G) {
+        while (ld_acquire(counters + st.dep) < (unsigned)G) {
           if (++spins > kEMaxSpin) {
             s_abort = 1;
             atomicExch(counters + hdr.n_ops, 1u);
@@ -433,25 +570,23 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
           }
           __nanosleep(64);
         }
-        __threadfence();
       }
-      __syncthreads();
-      if (s_abort) break;  // CTA-uniform
+      csync();
+      if (s_abort) break;  // same value in every consumer thread
       done_upto = st.dep;
     }
     etrace(si, 1);
     // ---- 2. activations ----
-    rotate_stage(st, cops, B, zs, scratch, warp, lane, tid, si);
+    rotate_stage(st, cops, B, zs, scratch, warp, lane, ctid, si);
     etrace(si, 6);
     etrace(si, 2);
 
-    // ---- 3. decode this warp's units ----
-    int wb, we;
-    warp_range(si, wb, we);
+    // ---- 3. decode this warp's units, two per iteration where possible ----
+    const int wb = static_cast<int>(v * T / V), we = static_cast<int>((v + 1) * T / V);
     if (wb < we) {
-      float acc[2][1][4];
+      float accA[2][1][4], accB[2][1][4];
       int cur_tile = -1;
-      uint32_t prevP1g = 0u, prevP1q = 0u;
+      uint32_t prevg = 0u, prevq = 0u;
       const uint4* zq = reinterpret_cast<const uint4*>(zs);
       const int zrow_q = st.d_pad / 8;  // one job row, in uint4
       int k = 0;                        // op (within the stage) of the current tile
@@ -463,74 +598,75 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
         for (int e = 0; e < 4; ++e) {
           const int bn = 2 * t + (e & 1);
           const int r = (tile - t0) * kTileRows + g + ((e < 2) ? 0 : 8);
-          if (bn < B) atomicAdd(&red[r * Bp + bn], acc[0][0][e] + acc[1][0][e]);
+          if (bn < B) atomicAdd(&red[r * Bp + bn], accA[0][0][e] + accA[1][0][e] + accB[0][0][e] + accB[1][0][e]);
         }
       };
       int tile = wb / st.units_k;
       int u = wb - tile * st.units_k;
-      for (int idx = wb; idx < we; ++idx) {
+      int idx = wb;
+      while (idx < we) {
         if (tile != cur_tile) {
           if (cur_tile >= 0) flush(cur_tile);
           cur_tile = tile;
           while (k < last_op && tile >= cops[k + 1].tile_base) ++k;
           zb = g < B ? (k * B + g) * zrow_q + t * 4 : static_cast<int>(hdr.zero_q);
 #pragma unroll
-          for (int q = 0; q < 2; ++q) acc[q][0][0] = acc[q][0][1] = acc[q][0][2] = acc[q][0][3] = 0.f;
-          prevP1g = prevP1q = 0u;
+          for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) accA[q][0][e] = accB[q][0][e] = 0.f;
+          prevg = prevq = 0u;
           if (u > 0) {  // trellis halo: last chunk of the previous unit of this row tile
             const EOp& op = cops[k];
             const uint4 pv = ldg_stream(op.stream + ((int64_t)(idx - 1 - op.unit_base) * 32 + lane) * BITS);
-            prevP1g = pv.z;
-            prevP1q = pv.w;
+            prevg = pv.z;
+            prevq = pv.w;
           }
         }
-        if (!mbar_wait(&s_bar[warp][slot], parity)) {
-          ok = false;
-          break;
-        }
-        uint4 cur[BITS];
-        const uint4* su = reinterpret_cast<const uint4*>(ring + (size_t)slot * kUnitBytes) + lane * BITS;
+        const int slot2 = slot + 1 == slots ? 0 : slot + 1;
+        const unsigned fph2 = slot + 1 == slots ? fph ^ 1u : fph;
+        if (idx + 1 < we && u + 1 < st.units_k) {
+          // two units of the same row tile: independent work for the scheduler
+          if (!mbar_wait(&s_full[warp][slot], fph) || !mbar_wait(&s_full[warp][slot2], fph2)) {
+            ok = false;
+            break;
+          }
+          uint4 ca[BITS], cb2[BITS];
+          const uint4* sa = reinterpret_cast<const uint4*>(ring + (size_t)slot * kUnitBytes) + lane * BITS;
+          const uint4* sb = reinterpret_cast<const uint4*>(ring + (size_t)slot2 * kUnitBytes) + lane * BITS;
 #pragma unroll
-        for (int q = 0; q < BITS; ++q) cur[q] = su[q];
-        __syncwarp();
-        if (lane == 0 && is < hdr.n_stages) {  // refill with the next unit of this warp's runs
-          fence_proxy_async();
-          issue(slot);
-        }
-        ++n_consumed;
-        if (++slot == slots) {
-          slot = 0;
-          parity ^= 1u;
-        }
-        const uint32_t P0g = cur[0].x, P0q = cur[0].y, P1g = cur[0].z, P1q = cur[0].w;
-        const uint32_t H0g = __shfl_sync(0xffffffffu, t == 3 ? prevP1g : P0g, src);
-        const uint32_t H0q = __shfl_sync(0xffffffffu, t == 3 ? prevP1q : P0q, src);
-        const uint32_t H1g = __shfl_sync(0xffffffffu, t == 3 ? P0g : P1g, src);
-        const uint32_t H1q = __shfl_sync(0xffffffffu, t == 3 ? P0q : P1q, src);
-        prevP1g = P1g;
-        prevP1q = P1q;
+          for (int q = 0; q < BITS; ++q) {
+            ca[q] = sa[q];
+            cb2[q] = sb[q];
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&s_empty[warp][slot]);
+            mbar_arrive(&s_empty[warp][slot2]);
+          }
+          slot = slot2 + 1 == slots ? 0 : slot2 + 1;
+          fph = slot2 + 1 == slots ? fph2 ^ 1u : fph2;
+          decode_unit<BITS, S>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
+          decode_unit<BITS, S>(lut, lanew, zq, cb2, prevg, prevq, t, src, zb + zu * (u * 32 + 32), zu * 16, accB);
+          u += 2;
+          idx += 2;
+        } else {
+          if (!mbar_wait(&s_full[warp][slot], fph)) {
+            ok = false;
+            break;
+          }
+          uint4 ca[BITS];
+          const uint4* sa = reinterpret_cast<const uint4*>(ring + (size_t)slot * kUnitBytes) + lane * BITS;
 #pragma unroll
-        for (int cgi = 0; cgi < 2; ++cgi) {
-          int zoff[1];
-          zoff[0] = zb + zu * (u * 32 + cgi * 16);
-          const uint32_t Pg = cgi ? P1g : P0g, Pq = cgi ? P1q : P0q;
-          const uint32_t Hg = cgi ? H1g : H0g, Hq = cgi ? H1q : H0q;
-          uint32_t Mg0 = 0u, Mq0 = 0u, Mg1 = 0u, Mq1 = 0u, Mg2 = 0u, Mq2 = 0u;
-          if (BITS >= 2) {
-            Mg0 = cgi ? cur[1].z : cur[1].x;
-            Mq0 = cgi ? cur[1].w : cur[1].y;
-          }
-          if (BITS >= 3) {
-            Mg1 = cgi ? cur[2].z : cur[2].x;
-            Mq1 = cgi ? cur[2].w : cur[2].y;
-          }
-          if (BITS >= 4) {
-            Mg2 = cgi ? cur[3].z : cur[3].x;
-            Mq2 = cgi ? cur[3].w : cur[3].y;
-          }
-          process_chunk<BITS, S, 1>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
+          for (int q = 0; q < BITS; ++q) ca[q] = sa[q];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_empty[warp][slot]);
+          slot = slot2;
+          fph = fph2;
+          decode_unit<BITS, S>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
+          u += 1;
+          idx += 1;
         }
-        if (++u == st.units_k) {
+        if (u == st.units_k) {
           u = 0;
           ++tile;
         }
@@ -542,49 +678,34 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
       atomicExch(counters + hdr.n_ops, 2u);
     }
     cp_async_wait_all();  // row scales / biases and the descriptors of stage si + 2
-    __syncthreads();
+    csync();
     etrace(si, 3);
 
     // ---- 4. publish: scaled tile partials into y, bias once per row ----
-    for (int i = tid; i < ntiles * kTileRows * B; i += kEThreads) {
-      const int bn = i / (ntiles * kTileRows);
-      const int rr = i - bn * ntiles * kTileRows;
-      const int tile_i = t0 + rr / kTileRows;
-      int kk = 0;
-      while (kk < st.n_ops - 1 && tile_i >= cops[kk + 1].tile_base) ++kk;
-      const EOp& op = cops[kk];
-      const int row = (tile_i - op.tile_base) * kTileRows + (rr % kTileRows);
-      const float part = red[rr * Bp + bn];
-      red[rr * Bp + bn] = 0.f;  // ready for the next stage
-      if (row >= op.n) continue;
-      float val = part * h2f_bits(s_sc[rr]);
-      const int first = tile_i * st.units_k;  // unit 0 of this row tile: its CTA adds the bias
-      if (first >= cb && first < ce) val += h2f_bits(s_bi[rr]);
-      atomicAdd(op.y + (int64_t)bn * op.n + row, val);
-    }
-    // CTA barrier, then one gpu-scope fence (cumulative over the writes the
-    // barrier ordered before it) ahead of the completion count
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      atomicAdd(counters + si, 1u);
-    }
-    etrace(si, 4);
-    if (s_abort) break;  // read after the barrier above: CTA-uniform
-  }
-
-  cp_async_wait_all();
-  // ---- drain copies still in flight (only after an abort) ----
-  if (lane == 0) {
-    while (n_consumed < n_issued) {
-      if (!mbar_wait(&s_bar[warp][slot], parity)) break;
-      ++n_consumed;
-      if (++slot == slots) {
-        slot = 0;
-        parity ^= 1u;
+    for (int bn = 0; bn < B; ++bn) {
+      for (int rr = ctid; rr < ntiles * kTileRows; rr += kECThreads) {
+        const int tile_i = t0 + (rr >> 4);
+        int kk = 0;
+        while (kk < st.n_ops - 1 && tile_i >= cops[kk + 1].tile_base) ++kk;
+        const EOp& op = cops[kk];
+        const int row = (tile_i - op.tile_base) * kTileRows + (rr & 15);
+        const float part = red[rr * Bp + bn];
+        red[rr * Bp + bn] = 0.f;  // ready for the next stage
+        if (row >= op.n) continue;
+        float val = part * h2f_bits(s_sc[rr]);
+        const int first = tile_i * st.units_k;  // unit 0 of this row tile: its CTA adds the bias
+        if (first >= cb && first < ce) val += h2f_bits(s_bi[rr]);
+        atomicAdd(op.y + (int64_t)bn * op.n + row, val);
       }
     }
+    // consumer barrier, then a release (cumulative over the writes the
+    // barrier ordered before it) ahead of the completion count
+    csync();
+    if (ctid == 0) red_release(counters + si);
+    etrace(si, 4);
+    if (s_abort) break;  // read after the barrier above: same in every consumer thread
   }
+  cp_async_wait_all();
 }
 
 int sm_count_e() {
@@ -698,20 +819,20 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
       while ((1 << lg) < s.block) ++lg;
       e.lg = lg;
       e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(s.block)));
-      const uintptr_t xa = s.x_dtype == TP_F32 ? 16 : 8;
-      e.vec = (s.d % 4 == 0 && aligned(s.x, xa)) ? 1 : 0;
+      // raw cp.async staging: 16-byte aligned rows of x and of rot_scale
+      e.vec = (s.d % 8 == 0 && aligned(s.x, 16)) ? 1 : 0;
       st.push_back(e);
     }
     stage_of[i] = static_cast<int>(st.size()) - 1;
     EStage& c = st.back();
     c.n_ops += 1;
-    if (!aligned(s.rot_scale, 8)) c.vec = 0;
+    if (!aligned(s.rot_scale, 16)) c.vec = 0;
   }
   const int n_stages = static_cast<int>(st.size());
   EHeader* h = static_cast<EHeader*>(image);
   EOp* eo = reinterpret_cast<EOp*>(h + 1);
   EStage* es = reinterpret_cast<EStage*>(eo + n_ops);
-  int64_t max_tiles = 1, zrows_q = 0, scratch_floats = 0;
+  int64_t max_tiles = 1, zrows_q = 0, scratch_bytes = 0;
   for (int si = 0; si < n_stages; ++si) {
     EStage& c = st[si];
     int64_t tiles = 0;
@@ -732,9 +853,15 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
     c.total_tiles = static_cast<int32_t>(tiles);
     c.total_units = static_cast<int32_t>(tiles * c.units_k);
     const int64_t jobs = (int64_t)c.n_ops * B;
-    c.rows_per_pass =
-        static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(jobs, kEScratchRowFloats / c.d_pad)));
-    scratch_floats = std::max<int64_t>(scratch_floats, (int64_t)c.rows_per_pass * c.d_pad);
+    // scratch: staged x rows (raw dtype, or fp32), rot_scale rows, fp32 work row
+    const int64_t xes = c.vec && c.x_dtype != TP_F32 ? 2 : 4;
+    c.rows_per_pass = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(B, kEXStageBytes / (c.d * xes))));
+    c.rs_off = static_cast<uint32_t>(pad_to((int64_t)c.rows_per_pass * c.d * xes, 16));
+    const int64_t rs_end = c.rs_off + pad_to((int64_t)c.n_ops * c.d * 2, 16);
+    // fp32 work row for blocks not done as one warp job
+    c.work_off = static_cast<uint32_t>(rs_end);
+    const int64_t work = (c.block > 1024 || c.block < 32) ? (int64_t)c.d * 4 : 0;
+    scratch_bytes = std::max<int64_t>(scratch_bytes, rs_end + work);
     zrows_q = std::max<int64_t>(zrows_q, jobs * c.d_pad / 8);
     const int64_t per_cta = (kEWarps * (int64_t)c.total_units + V - 1) / V;
     max_tiles = std::max<int64_t>(max_tiles, per_cta / c.units_k + 2);
@@ -753,7 +880,7 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   hh.zero_q = static_cast<uint32_t>(zrows_q);  // 64 zero bytes after the widest stage's rows
   const uint32_t lut = bits == 4 ? LutCfg<4>::kLutBytes : LutCfg<3>::kLutBytes;
   const uint64_t zbytes = (uint64_t)zrows_q * 16 + 64;
-  const uint64_t scratch = (uint64_t)scratch_floats * 4;
+  const uint64_t scratch = (uint64_t)scratch_bytes;
   const uint64_t red = (uint64_t)max_tiles * kTileRows * 8 * 4;
   const uint64_t rowc = (uint64_t)max_tiles * kTileRows * 2 * 2;  // row scales + biases
   const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red) + al128(rowc);
