@@ -229,9 +229,46 @@ TP_API int64_t tp_engine_image_bytes(int n_ops);
 TP_API tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, int bits, int n_states,
                                  const uint16_t* codebook, void* image, int64_t image_bytes);
 
-/* Bytes of the counter block (n_ops + 1 words); zero it before each run.
- * After a run, word n_ops is non-zero if a wait timed out. */
+/* Bytes of the counter block (n_ops + 2 words).  On one GPU zero it before
+ * each run; after a run, word n_ops is non-zero if a wait timed out. */
 TP_API int64_t tp_engine_counter_bytes(int n_ops);
+
+/* Tensor-parallel program over n_ranks GPUs of one node (one process per
+ * GPU).  Each rank runs a shard of every op (a 16-row-aligned range of its
+ * output rows: ops[i].n rows starting at row0[i] of n_full[i]) and adds its
+ * partial outputs into EVERY rank's copy of the output with fp32 atomics over
+ * NVLink peer mappings, then counts completion on every rank; a stage waits
+ * until every CTA of every rank has published its input.  This is the
+ * all-gather / all-reduce of the layer outputs fused into the GEMV epilogue
+ * (no separate collective).  Outputs live in a double-buffered arena that
+ * every rank maps: ops[i].y and a dependent ops[i].x are BYTE OFFSETS into
+ * one arena buffer; run r writes buffer r % 2 and clears the other.  The
+ * counter block must be peer-mapped too, zeroed once before the first run and
+ * never again (counts are cumulative).  Before the first run every rank must
+ * have zeroed both arena buffers (then synchronise the ranks). */
+typedef struct tp_engine_tp {
+  int32_t n_ranks, rank;
+  void* arena[2];                  /* this rank's two arena buffers (16-byte aligned)       */
+  int64_t arena_bytes;             /* bytes of one buffer (multiple of 16)                   */
+  const uint64_t* peer_arena;      /* device array [n_ranks][2]: every rank's buffers here   */
+  unsigned* const* peer_counters;  /* device array [n_ranks]: every rank's counter block     */
+} tp_engine_tp;
+
+TP_API tp_status tp_engine_build_tp(const tp_engine_op* ops, const int64_t* row0, const int64_t* n_full,
+                                    int n_ops, int B, int bits, int n_states, const uint16_t* codebook,
+                                    const tp_engine_tp* tp, void* image, int64_t image_bytes);
+
+/* Peer memory for tensor-parallel programs (CUDA IPC within one node).
+ * tp_ipc_alloc: zero-filled device allocation whose IPC handle covers
+ * exactly it (the fill completes before the call returns);
+ * tp_ipc_get_handle writes TP_IPC_HANDLE_BYTES bytes; tp_ipc_open maps a
+ * peer's allocation into this process (the current device). */
+#define TP_IPC_HANDLE_BYTES 64
+TP_API tp_status tp_ipc_alloc(int64_t bytes, void** ptr);
+TP_API tp_status tp_ipc_free(void* ptr);
+TP_API tp_status tp_ipc_get_handle(void* ptr, void* handle);
+TP_API tp_status tp_ipc_open(const void* handle, void** ptr);
+TP_API tp_status tp_ipc_close(void* ptr);
 
 /* Run the program on `stream` (image_dev: device copy; image_host: the
  * host image it was copied from). */

@@ -47,6 +47,12 @@ SIGNATURES: dict[str, tuple] = {
     "tp_engine_build": (_I, [_P, _I, _I, _I, _I, _P, _P, _I64]),
     "tp_engine_counter_bytes": (_I64, [_I]),
     "tp_engine_run": (_I, [_P, _P, _P, _P]),
+    "tp_engine_build_tp": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I64]),
+    "tp_ipc_alloc": (_I, [_I64, _P]),
+    "tp_ipc_free": (_I, [_P]),
+    "tp_ipc_get_handle": (_I, [_P, _P]),
+    "tp_ipc_open": (_I, [_P, _P]),
+    "tp_ipc_close": (_I, [_P]),
     "tp_gemv_v2": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _I, _P]),
 }
 

@@ -61,9 +61,10 @@ struct alignas(16) EOp {
   const uint16_t* scales;
   const uint16_t* bias;
   const uint16_t* rot_scale;
-  float* y;
-  int32_t n, tile_base;  // first row tile of this op inside its stage
-  int32_t unit_base, pad0;
+  uint64_t y;            // fp32 output: address (single GPU) or byte offset into the arena (tensor parallel)
+  int32_t n, tile_base;  // rows decoded here; first row tile of this op inside its stage
+  int32_t unit_base, r0;  // first unit inside the stage; first output row of this shard
+  int32_t n_full, pad0;   // rows of the full output (row stride of y)
 };
 
 struct alignas(16) EStage {
@@ -82,6 +83,14 @@ struct alignas(16) EHeader {
   const uint16_t* codebook;
   uint32_t ring_off, z_off, scratch_off, red_off;
   uint32_t smem, zero_q, max_tiles, sc_off;  // sc_off: per-CTA row scales, then biases (fp16)
+  // tensor parallel (n_ranks > 1): outputs live in a double-buffered arena
+  // replicated on every rank; every CTA adds its partials into all ranks'
+  // copies and counts completion on all ranks (peer pointers, NVLink).
+  int32_t n_ranks, rank;
+  uint64_t arena[2];             // this rank's arena buffers (0 on one GPU: op.y is an address)
+  uint64_t arena_bytes;          // bytes of one arena buffer
+  const uint64_t* peer_arena;    // [n_ranks][2] arena buffer addresses on every rank
+  unsigned* const* peer_ctr;     // [n_ranks] counter blocks on every rank
 };
 
 static_assert(sizeof(EOp) == 64 && sizeof(EStage) % 16 == 0 && sizeof(EHeader) % 16 == 0, "image layout");
@@ -112,6 +121,15 @@ __device__ __forceinline__ float load_x(const EStage& st, int64_t i) {
 // completion counters: release increment / acquire read at gpu scope
 __device__ __forceinline__ void red_release(unsigned* p) {
   asm volatile("fence.acq_rel.gpu;\n red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+}
+__device__ __forceinline__ void red_release_sys(unsigned* const* ctrs, int n, int idx) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int p = 0; p < n; ++p) asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(ctrs[p] + idx) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -404,6 +422,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   __shared__ __align__(16) EOp s_ops[3][kEMaxStageOps];  // descriptors of stages si, si+1, si+2
   __shared__ __align__(16) EStage s_st[3];
   __shared__ int s_abort;
+  __shared__ unsigned s_epoch;
 
   const EHeader hdr = *hdr_g;
   const EOp* ops = reinterpret_cast<const EOp*>(hdr_g + 1);
@@ -522,6 +541,24 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
 
   // ===================== consumer warps =====================
   const int ctid = tid;
+  const int P = hdr.n_ranks;
+  // epoch = runs of this program so far (each CTA counts itself once per run;
+  // counters are never cleared between runs on several ranks)
+  if (ctid == 0) s_epoch = atomicAdd(counters + hdr.n_ops + 1, 1u) / (unsigned)G;
+  csync();
+  const unsigned epoch = s_epoch;
+  const unsigned target = (unsigned)G * (unsigned)P * (epoch + 1u);  // stage complete on every CTA of every rank
+  const int buf_y = P > 1 ? (int)(epoch & 1u) : 0;
+  if (P > 1) {
+    // clear the arena buffer the NEXT run writes into: every rank finished
+    // writing it (the previous run's last stage completed everywhere before
+    // this kernel started), and peers write it again only after this run
+    uint4* nz = reinterpret_cast<uint4*>(hdr.arena[buf_y ^ 1]);
+    const uint64_t n16 = hdr.arena_bytes / 16;
+    for (uint64_t i = (uint64_t)blockIdx.x * kECThreads + ctid; i < n16; i += (uint64_t)G * kECThreads)
+      nz[i] = make_uint4(0u, 0u, 0u, 0u);
+    csync();
+  }
   const int64_t v = (int64_t)blockIdx.x * kEWarps + warp;
   const unsigned char* ring = smem + hdr.ring_off + (size_t)warp * slots * kUnitBytes;
   int slot = 0;
@@ -533,7 +570,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   prefetch_stage(s_st[0], s_ops[0], v, V, lane, ctid, kUnitBytes);
   for (int si = 0, buf = 0; si < hdr.n_stages; ++si, buf = buf == 2 ? 0 : buf + 1) {
     bool ok = true;  // this warp's copies landed
-    const EStage st = s_st[buf];
+    EStage st = s_st[buf];
+    if (st.dep >= 0) st.x = reinterpret_cast<const void*>(hdr.arena[buf_y] + reinterpret_cast<uint64_t>(st.x));
     const EOp* cops = s_ops[buf];
     const int nbuf = buf == 2 ? 0 : buf + 1;
     etrace(si, 0);
@@ -562,7 +600,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     if (st.dep > done_upto) {
       if (ctid == 0) {
         unsigned spins = 0;
-        while (ld_acquire(counters + st.dep) < (unsigned)G) {
+        while ((P > 1 ? ld_acquire_sys(counters + st.dep) : ld_acquire(counters + st.dep)) < target) {
           if (++spins > kEMaxSpin) {
             s_abort = 1;
             atomicExch(counters + hdr.n_ops, 1u);
@@ -695,17 +733,37 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
         float val = part * h2f_bits(s_sc[rr]);
         const int first = tile_i * st.units_k;  // unit 0 of this row tile: its CTA adds the bias
         if (first >= cb && first < ce) val += h2f_bits(s_bi[rr]);
-        atomicAdd(op.y + (int64_t)bn * op.n + row, val);
+        const uint64_t off = op.y + 4ull * ((uint64_t)bn * op.n_full + op.r0 + row);
+        if (P == 1) {
+          atomicAdd(reinterpret_cast<float*>(off), val);
+        } else {
+          for (int pr = 0; pr < P; ++pr) atomicAdd(reinterpret_cast<float*>(hdr.peer_arena[2 * pr + buf_y] + off), val);
+        }
       }
     }
     // consumer barrier, then a release (cumulative over the writes the
     // barrier ordered before it) ahead of the completion count
     csync();
-    if (ctid == 0) red_release(counters + si);
+    if (ctid == 0) {
+      if (P == 1) red_release(counters + si);
+      else red_release_sys(hdr.peer_ctr, P, si);
+    }
     etrace(si, 4);
     if (s_abort) break;  // read after the barrier above: same in every consumer thread
   }
   cp_async_wait_all();
+  if (P > 1 && ctid == 0 && !s_abort) {
+    // peers may still be adding into this rank's arena: leave only when the
+    // last stage is complete everywhere (the next run clears this buffer's twin)
+    unsigned spins = 0;
+    while (ld_acquire_sys(counters + hdr.n_stages - 1) < target) {
+      if (++spins > kEMaxSpin) {
+        atomicExch(counters + hdr.n_ops, 1u);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
 }
 
 int sm_count_e() {
@@ -764,12 +822,23 @@ extern "C" int64_t tp_engine_image_bytes(int n_ops) {
 
 extern "C" int64_t tp_engine_counter_bytes(int n_ops) {
   if (n_ops < 1) return -1;
-  return (int64_t)(n_ops + 1) * 4;
+  return (int64_t)(n_ops + 2) * 4;
 }
 
-extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, int bits, int n_states,
-                                     const uint16_t* codebook, void* image, int64_t image_bytes) {
+namespace {
+// row0 / n_full: first output row and full output rows of every op (shards
+// of a tensor-parallel program), or null (whole ops).  tp: null on one GPU.
+tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t* n_full, int n_ops, int B, int bits,
+                     int n_states, const uint16_t* codebook, const tp_engine_tp* tp, void* image,
+                     int64_t image_bytes) {
   if (!ops || n_ops < 1 || !codebook || !image) return fail(TP_ERR_ARG, "tp_engine_build: bad arguments");
+  const int P = tp ? tp->n_ranks : 1;
+  if (tp && (P < 2 || P > 64 || tp->rank < 0 || tp->rank >= P || !tp->arena[0] || !tp->arena[1] ||
+             !tp->peer_arena || !tp->peer_counters || tp->arena_bytes <= 0 || tp->arena_bytes % 16 ||
+             !aligned(tp->arena[0], 16) || !aligned(tp->arena[1], 16)))
+    return fail(TP_ERR_ARG, "tp_engine_build_tp: bad tensor-parallel description");
+  auto full_rows = [&](int i) { return n_full ? n_full[i] : ops[i].n; };
+  auto first_row = [&](int i) { return row0 ? row0[i] : (int64_t)0; };
   if (image_bytes < tp_engine_image_bytes(n_ops)) return fail(TP_ERR_ARG, "tp_engine_build: image too small");
   if (!aligned(image, 16)) return fail(TP_ERR_ALIGN, "tp_engine_build: image must be 16-byte aligned");
   if (B < 1 || B > kEMaxB) return fail(TP_ERR_UNSUPPORTED, "engine: batch must be 1..%d (got %d)", kEMaxB, B);
@@ -779,14 +848,20 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   const int64_t V = (int64_t)G * kEWarps;
   for (int i = 0; i < n_ops; ++i) {
     const tp_engine_op& s = ops[i];
-    if (!s.tcq_stream || !s.scales || !s.rot_scale || !s.x || !s.y || s.n < 1 || s.d < 1)
+    // on several ranks y (and a dependent x) are byte offsets into the arena
+    if (!s.tcq_stream || !s.scales || !s.rot_scale || (!tp && (!s.x || !s.y)) || (tp && s.dep < 0 && !s.x) ||
+        s.n < 1 || s.d < 1)
       return fail(TP_ERR_ARG, "engine op %d: bad arguments", i);
+    if (first_row(i) < 0 || first_row(i) + s.n > full_rows(i) || first_row(i) % kTileRows)
+      return fail(TP_ERR_ARG, "engine op %d: shard rows out of range or not 16-row aligned", i);
+    if (tp && ((uint64_t)(uintptr_t)s.y % 16 || (uint64_t)(uintptr_t)s.y + full_rows(i) * B * 4 > (uint64_t)tp->arena_bytes))
+      return fail(TP_ERR_ARG, "engine op %d: output outside the arena", i);
     if (!aligned(s.tcq_stream, 16)) return fail(TP_ERR_ALIGN, "engine op %d: stream must be 16-byte aligned", i);
     if (!aligned(s.scales, 4) || (s.bias && !aligned(s.bias, 4)))
       return fail(TP_ERR_ALIGN, "engine op %d: scales and bias must be 4-byte aligned", i);
     if (!valid_dtype(s.x_dtype)) return fail(TP_ERR_ARG, "engine op %d: bad x dtype", i);
     if (s.dep >= i || s.dep < -1) return fail(TP_ERR_ARG, "engine op %d: dep must be -1 or an earlier op", i);
-    if (s.dep >= 0 && (s.x_dtype != TP_F32 || ops[s.dep].n != s.d || s.x != ops[s.dep].y))
+    if (s.dep >= 0 && (s.x_dtype != TP_F32 || full_rows(s.dep) != s.d || s.x != ops[s.dep].y))
       return fail(TP_ERR_ARG, "engine op %d: a dependent input must be op %d's fp32 output", i, s.dep);
     if (s.block < 1 || s.block > 8192 || (s.block & (s.block - 1)) || s.d % s.block)
       return fail(TP_ERR_UNSUPPORTED, "engine op %d: Hadamard block %d unsupported (1..8192)", i, s.block);
@@ -842,8 +917,10 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
       e.scales = ops[i].scales;
       e.bias = ops[i].bias;
       e.rot_scale = ops[i].rot_scale;
-      e.y = ops[i].y;
+      e.y = reinterpret_cast<uint64_t>(ops[i].y);
       e.n = static_cast<int32_t>(ops[i].n);
+      e.r0 = static_cast<int32_t>(first_row(i));
+      e.n_full = static_cast<int32_t>(full_rows(i));
       e.tile_base = static_cast<int32_t>(tiles);
       e.unit_base = static_cast<int32_t>(tiles * c.units_k);
       eo[i] = e;
@@ -875,6 +952,15 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   hh.bits = bits;
   hh.n_states = n_states;
   hh.grid = G;
+  hh.n_ranks = P;
+  hh.rank = tp ? tp->rank : 0;
+  if (tp) {
+    hh.arena[0] = reinterpret_cast<uint64_t>(tp->arena[0]);
+    hh.arena[1] = reinterpret_cast<uint64_t>(tp->arena[1]);
+    hh.arena_bytes = static_cast<uint64_t>(tp->arena_bytes);
+    hh.peer_arena = tp->peer_arena;
+    hh.peer_ctr = tp->peer_counters;
+  }
   hh.codebook = codebook;
   hh.max_tiles = static_cast<uint32_t>(max_tiles);
   hh.zero_q = static_cast<uint32_t>(zrows_q);  // 64 zero bytes after the widest stage's rows
@@ -898,6 +984,19 @@ extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, 
   hh.smem = al128(hh.sc_off + rowc);
   *h = hh;
   return clear_ok();
+}
+}  // namespace
+
+extern "C" tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, int bits, int n_states,
+                                     const uint16_t* codebook, void* image, int64_t image_bytes) {
+  return build_impl(ops, nullptr, nullptr, n_ops, B, bits, n_states, codebook, nullptr, image, image_bytes);
+}
+
+extern "C" tp_status tp_engine_build_tp(const tp_engine_op* ops, const int64_t* row0, const int64_t* n_full,
+                                        int n_ops, int B, int bits, int n_states, const uint16_t* codebook,
+                                        const tp_engine_tp* tp, void* image, int64_t image_bytes) {
+  if (!tp || !row0 || !n_full) return fail(TP_ERR_ARG, "tp_engine_build_tp: bad arguments");
+  return build_impl(ops, row0, n_full, n_ops, B, bits, n_states, codebook, tp, image, image_bytes);
 }
 
 extern "C" tp_status tp_engine_run(const void* image_dev, const void* image_host, unsigned* counters, void* stream) {
