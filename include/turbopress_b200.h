@@ -229,8 +229,8 @@ TP_API int64_t tp_engine_image_bytes(int n_ops);
 TP_API tp_status tp_engine_build(const tp_engine_op* ops, int n_ops, int B, int bits, int n_states,
                                  const uint16_t* codebook, void* image, int64_t image_bytes);
 
-/* Bytes of the counter block (n_ops + 2 words).  On one GPU zero it before
- * each run; after a run, word n_ops is non-zero if a wait timed out. */
+/* Bytes of the counter block (2 * n_ops + 2 words).  On one GPU zero it
+ * before each run; after a run, word n_ops is non-zero if a wait timed out. */
 TP_API int64_t tp_engine_counter_bytes(int n_ops);
 
 /* Tensor-parallel program over n_ranks GPUs of one node (one process per

@@ -122,6 +122,13 @@ __device__ __forceinline__ float load_x(const EStage& st, int64_t i) {
 __device__ __forceinline__ void red_release(unsigned* p) {
   asm volatile("fence.acq_rel.gpu;\n red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
 }
+// gpu-scope acq_rel increment returning the old count
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+  return old;
+}
+// one system-scope release, then +1 on word idx of every rank's counter block
 __device__ __forceinline__ void red_release_sys(unsigned* const* ctrs, int n, int idx) {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
   for (int p = 0; p < n; ++p) asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(ctrs[p] + idx) : "memory");
@@ -547,7 +554,13 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   if (ctid == 0) s_epoch = atomicAdd(counters + hdr.n_ops + 1, 1u) / (unsigned)G;
   csync();
   const unsigned epoch = s_epoch;
-  const unsigned target = (unsigned)G * (unsigned)P * (epoch + 1u);  // stage complete on every CTA of every rank
+  // On one GPU a stage is complete when its counter reaches G (cleared per
+  // run).  On several ranks every CTA counts on its own GPU (word si), and the
+  // last CTA of each rank to finish a stage counts once on every rank (word
+  // n_ops + 2 + si): complete when that reaches P per run so far.
+  const unsigned local_target = (unsigned)G * (epoch + 1u);
+  const unsigned target = P > 1 ? (unsigned)P * (epoch + 1u) : (unsigned)G;
+  unsigned* const gctr = P > 1 ? counters + hdr.n_ops + 2 : counters;
   const int buf_y = P > 1 ? (int)(epoch & 1u) : 0;
   if (P > 1) {
     // clear the arena buffer the NEXT run writes into: every rank finished
@@ -600,7 +613,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     if (st.dep > done_upto) {
       if (ctid == 0) {
         unsigned spins = 0;
-        while ((P > 1 ? ld_acquire_sys(counters + st.dep) : ld_acquire(counters + st.dep)) < target) {
+        while ((P > 1 ? ld_acquire_sys(gctr + st.dep) : ld_acquire(counters + st.dep)) < target) {
           if (++spins > kEMaxSpin) {
             s_abort = 1;
             atomicExch(counters + hdr.n_ops, 1u);
@@ -745,8 +758,14 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     // barrier ordered before it) ahead of the completion count
     csync();
     if (ctid == 0) {
-      if (P == 1) red_release(counters + si);
-      else red_release_sys(hdr.peer_ctr, P, si);
+      if (P == 1) {
+        red_release(counters + si);
+      } else if (atom_add_acq_rel(counters + si) + 1u == local_target) {
+        // last CTA of this rank: its acquire saw every local CTA's release
+        // (which covered that CTA's adds into the peers' copies), so one
+        // system-scope release publishes the whole rank's stage
+        red_release_sys(hdr.peer_ctr, P, hdr.n_ops + 2 + si);
+      }
     }
     etrace(si, 4);
     if (s_abort) break;  // read after the barrier above: same in every consumer thread
@@ -756,7 +775,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
     // peers may still be adding into this rank's arena: leave only when the
     // last stage is complete everywhere (the next run clears this buffer's twin)
     unsigned spins = 0;
-    while (ld_acquire_sys(counters + hdr.n_stages - 1) < target) {
+    while (ld_acquire_sys(gctr + hdr.n_stages - 1) < target) {
       if (++spins > kEMaxSpin) {
         atomicExch(counters + hdr.n_ops, 1u);
         break;
@@ -822,7 +841,7 @@ extern "C" int64_t tp_engine_image_bytes(int n_ops) {
 
 extern "C" int64_t tp_engine_counter_bytes(int n_ops) {
   if (n_ops < 1) return -1;
-  return (int64_t)(n_ops + 2) * 4;
+  return (int64_t)(2 * n_ops + 2) * 4;
 }
 
 namespace {
