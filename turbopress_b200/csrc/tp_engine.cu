@@ -50,7 +50,7 @@ constexpr int kEMaxB = 4;
 constexpr int kEMaxSlots = TP_EMAXSLOTS;
 constexpr int kEMaxStageOps = 8;
 constexpr int kEXStageBytes = 48 * 1024;   // staged x rows per pass
-constexpr int kEZStageBytes = 48 * 1024;   // activations of one stage (grouping cap)
+constexpr int kEZStageBytes = 48 * 1024;   // activations + rot_scale rows of one stage (grouping cap)
 constexpr unsigned kEMaxSpin = 1u << 24;   // dependency polls (~1 s with backoff)
 constexpr unsigned kEMaxIdle = 1u << 25;   // producer polls without progress (~4 s)
 constexpr int kEMagic = 0x54504533;        // "TPE3"
@@ -315,32 +315,38 @@ __device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* z
         }
       }
     } else {
-      // one job at a time through the fp32 work row
+      // one Hadamard block at a time through the fp32 work row: blocks above
+      // 1024 as 512-wide warp transforms plus consumer-wide passes over the
+      // upper index bits, blocks below 32 consumer-wide
       float* work = reinterpret_cast<float*>(scr + st.work_off);
       for (int j = 0; j < st.n_ops; ++j)
-        for (int rr = 0; rr < rows; ++rr) {
-          for (int c = ctid; c < st.d; c += kECThreads)
-            work[c] = xs_at(scr, dt, rr * st.d + c) * h2f_bits(rs[j * st.d + c]);
-          csync();
-          int b_start = 0;
-          if (st.block > 1024) {
-            for (int sb = warp; sb < st.d / 512; sb += kEWarps) {
-              float v[16];
+        for (int rr = 0; rr < rows; ++rr)
+          for (int kb = 0; kb < nblk; ++kb) {
+            const int c0 = kb * st.block;
+            for (int c = ctid; c < st.block; c += kECThreads)
+              work[c] = xs_at(scr, dt, rr * st.d + c0 + c) * h2f_bits(rs[j * st.d + c0 + c]);
+            csync();
+            int b_start = 0;
+            if (st.block > 1024) {
+              for (int sb = warp; sb < st.block / 512; sb += kEWarps) {
+                float v[16];
 #pragma unroll
-              for (int r = 0; r < 16; ++r) v[r] = work[sb * 512 + lane + 32 * r];
-              warp_fwht_regs<16>(v, lane);
+                for (int r = 0; r < 16; ++r) v[r] = work[sb * 512 + lane + 32 * r];
+                warp_fwht_regs<16>(v, lane);
 #pragma unroll
-              for (int r = 0; r < 16; ++r) work[sb * 512 + lane + 32 * r] = v[r];
+                for (int r = 0; r < 16; ++r) work[sb * 512 + lane + 32 * r] = v[r];
+              }
+              csync();
+              b_start = 9;
+            }
+            fwht_consumers(work, st.block, b_start, st.lg, ctid);
+            __half* zrow = zs + (size_t)(j * B + b0 + rr) * st.d_pad;
+            for (int c = ctid; c < st.block; c += kECThreads) {
+              const int cc = c0 + c;  // the permutation works on absolute 32-column chunks
+              zrow[(cc & ~31) + zperm_pos(cc & 31)] = __float2half_rn(work[c] * st.norm);
             }
             csync();
-            b_start = 9;
           }
-          fwht_consumers(work, st.d, b_start, st.lg, ctid);
-          __half* zrow = zs + (size_t)(j * B + b0 + rr) * st.d_pad;
-          for (int c = ctid; c < st.d; c += kECThreads)
-            zrow[(c & ~31) + zperm_pos(c & 31)] = __float2half_rn(work[c] * st.norm);
-          csync();
-        }
     }
     csync();
   }
@@ -897,7 +903,8 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
       const EStage& c = st.back();
       const tp_engine_op& f = ops[c.first_op];
       join = f.x == s.x && f.x_dtype == s.x_dtype && f.dep == s.dep && f.d == s.d && f.block == s.block &&
-             c.n_ops < kEMaxStageOps && (int64_t)(c.n_ops + 1) * B * d_pad * 2 <= kEZStageBytes;
+             c.n_ops < kEMaxStageOps &&
+             (int64_t)(c.n_ops + 1) * (B * d_pad * 2 + s.d * 2) <= kEZStageBytes;  // activations + rot_scale rows
     }
     if (!join) {
       EStage e{};
@@ -956,7 +963,7 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
     const int64_t rs_end = c.rs_off + pad_to((int64_t)c.n_ops * c.d * 2, 16);
     // fp32 work row for blocks not done as one warp job
     c.work_off = static_cast<uint32_t>(rs_end);
-    const int64_t work = (c.block > 1024 || c.block < 32) ? (int64_t)c.d * 4 : 0;
+    const int64_t work = (c.block > 1024 || c.block < 32) ? (int64_t)c.block * 4 : 0;
     scratch_bytes = std::max<int64_t>(scratch_bytes, rs_end + work);
     zrows_q = std::max<int64_t>(zrows_q, jobs * c.d_pad / 8);
     const int64_t per_cta = (kEWarps * (int64_t)c.total_units + V - 1) / V;
