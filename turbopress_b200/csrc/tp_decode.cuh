@@ -175,7 +175,17 @@ __device__ __forceinline__ uint32_t x4(uint32_t M2, int w, int q, uint32_t lanep
   return (__funnelshift_r(M2, M2, s) & 0x01800180u) | lanepat;
 }
 
-template <int BITS, int S, int NT>
+// pair-table lookup at an absolute shared-window address
+__device__ __forceinline__ uint32_t lds_abs(uint32_t addr) {
+  uint32_t v;
+  asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// ABS (bits <= 3 only): the pair table sits at shared-window address
+// 0x10000 and `lanew` carries 0x10000 | lane*4, so one byte permute forms the
+// final address (byte 2 from lanew) and no base add is needed.
+template <int BITS, int S, int NT, bool ABS = false>
 __device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t lanew, const uint4* zq,
                                               uint32_t Pg, uint32_t Hg, uint32_t Pq, uint32_t Hq, uint32_t Mg0,
                                               uint32_t Mg1, uint32_t Mg2, uint32_t Mq0, uint32_t Mq1, uint32_t Mq2,
@@ -197,12 +207,21 @@ __device__ __forceinline__ void process_chunk(const unsigned char* lut, uint32_t
     for (int q = 0; q < 2; ++q) {
       uint32_t a0, a1, a2, a3;
       if (BITS <= 3) {
-        // [lane*4, level byte, 0, 0] = byte*256 + lane*4
-        const uint32_t s0 = 0x5504u | ((2u * q) << 4), s1 = 0x5504u | ((2u * q + 1u) << 4);
-        a0 = lds32(lut, prmt(Lg[w], lanew, s0));
-        a2 = lds32(lut, prmt(Lg[w], lanew, s1));
-        a1 = lds32(lut, prmt(Lq[w], lanew, s0));
-        a3 = lds32(lut, prmt(Lq[w], lanew, s1));
+        if (ABS) {
+          // [lane*4, level byte, 0x01, 0] = 0x10000 + byte*256 + lane*4
+          const uint32_t s0 = 0x7604u | ((2u * q) << 4), s1 = 0x7604u | ((2u * q + 1u) << 4);
+          a0 = lds_abs(prmt(Lg[w], lanew, s0));
+          a2 = lds_abs(prmt(Lg[w], lanew, s1));
+          a1 = lds_abs(prmt(Lq[w], lanew, s0));
+          a3 = lds_abs(prmt(Lq[w], lanew, s1));
+        } else {
+          // [lane*4, level byte, 0, 0] = byte*256 + lane*4
+          const uint32_t s0 = 0x5504u | ((2u * q) << 4), s1 = 0x5504u | ((2u * q + 1u) << 4);
+          a0 = lds32(lut, prmt(Lg[w], lanew, s0));
+          a2 = lds32(lut, prmt(Lg[w], lanew, s1));
+          a1 = lds32(lut, prmt(Lq[w], lanew, s0));
+          a3 = lds32(lut, prmt(Lq[w], lanew, s1));
+        }
       } else {
         const uint32_t xg = x4(Mg2, w, q, lanew), xq = x4(Mq2, w, q, lanew);
         const uint32_t s0 = 0xD504u | ((2u * q) << 4), s1 = 0xF706u | ((2u * q + 1u) << 4);

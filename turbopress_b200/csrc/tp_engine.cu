@@ -28,6 +28,7 @@
 //   4. scale (and bias, once per row) the CTA's tile partials and add them
 //      to the ops' fp32 outputs with atomics; publish completion.
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 #include "tp_decode.cuh"
@@ -83,6 +84,8 @@ struct alignas(16) EHeader {
   const uint16_t* codebook;
   uint32_t ring_off, z_off, scratch_off, red_off;
   uint32_t smem, zero_q, max_tiles, sc_off;  // sc_off: per-CTA row scales, then biases (fp16)
+  uint32_t lut_off, lut_abs;  // pair table offset; 1: it sits at shared-window address 0x10000
+  uint32_t dyn_base, pad_h;   // expected shared-window address of the dynamic area (lut_abs)
   // tensor parallel (n_ranks > 1): outputs live in a double-buffered arena
   // replicated on every rank; every CTA adds its partials into all ranks'
   // copies and counts completion on all ranks (peer pointers, NVLink).
@@ -392,7 +395,7 @@ __device__ void prefetch_stage(const EStage& nx, const EOp* nops, int64_t v, int
 
 // One unit (two 32-column chunks per lane) into `acc`; `prevg/prevq` carry
 // the trellis halo (last path words of the previous unit of the row tile).
-template <int BITS, int S>
+template <int BITS, int S, bool ABS>
 __device__ __forceinline__ void decode_unit(const unsigned char* lut, uint32_t lanew, const uint4* zq,
                                             const uint4 (&cur)[BITS], uint32_t& prevg, uint32_t& prevq, int t,
                                             int src, int zoff0, int zstep, float (*acc)[1][4]) {
@@ -422,11 +425,11 @@ __device__ __forceinline__ void decode_unit(const unsigned char* lut, uint32_t l
       Mg2 = cgi ? cur[3].z : cur[3].x;
       Mq2 = cgi ? cur[3].w : cur[3].y;
     }
-    process_chunk<BITS, S, 1>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
+    process_chunk<BITS, S, 1, ABS>(lut, lanew, zq, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, zoff, acc);
   }
 }
 
-template <int BITS, int S>
+template <int BITS, int S, bool ABS>
 __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader* __restrict__ hdr_g,
                                                                   unsigned* __restrict__ counters) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -446,7 +449,17 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const int64_t V = (int64_t)G * kEWarps;
   const int B = hdr.B, Bp = 8;
   constexpr unsigned kUnitBytes = 32u * 16u * BITS;
-  unsigned char* lut = smem;
+  unsigned char* lut = smem + hdr.lut_off;
+  if (ABS) {
+    // the absolute pair-table addresses assume this layout: check it before
+    // touching any shared memory, and give up (status 3) if it differs
+    unsigned dsz;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsz));
+    if (smem_u32(smem) != hdr.dyn_base || smem_u32(lut) != 0x10000u || hdr.lut_off + 65536u > dsz) {
+      if (threadIdx.x == 0) atomicExch(counters + hdr.n_ops, 3u);
+      return;
+    }
+  }
   __half* zs = reinterpret_cast<__half*>(smem + hdr.z_off);
   unsigned char* scratch = smem + hdr.scratch_off;
   float* red = reinterpret_cast<float*>(smem + hdr.red_off);
@@ -470,6 +483,15 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
 
   const uint32_t cbv = lane < (1 << (BITS + 1)) ? hdr.codebook[lane] : 0u;
   if (tid == 0) s_abort = 0;
+#ifdef TP_TRACE
+  if (tid == 0 && blockIdx.x == 0) {
+    unsigned dsz;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsz));
+    g_etrace[0][511][0] = smem_u32(smem);
+    g_etrace[0][511][1] = dsz;
+    g_etrace[0][511][2] = smem_u32(&s_full[0][0]);
+  }
+#endif
   if (tid < kEWarps * kEMaxSlots) {
     mbar_init(&s_full[0][0] + tid, 1);
     mbar_init(&s_empty[0][0] + tid, 1);
@@ -568,11 +590,12 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const unsigned target = P > 1 ? (unsigned)P * (epoch + 1u) : (unsigned)G;
   unsigned* const gctr = P > 1 ? counters + hdr.n_ops + 2 : counters;
   const int buf_y = P > 1 ? (int)(epoch & 1u) : 0;
+  const uint64_t arena_y = buf_y ? hdr.arena[1] : hdr.arena[0];  // (select: no dynamic index into hdr)
   if (P > 1) {
     // clear the arena buffer the NEXT run writes into: every rank finished
     // writing it (the previous run's last stage completed everywhere before
     // this kernel started), and peers write it again only after this run
-    uint4* nz = reinterpret_cast<uint4*>(hdr.arena[buf_y ^ 1]);
+    uint4* nz = reinterpret_cast<uint4*>(buf_y ? hdr.arena[0] : hdr.arena[1]);
     const uint64_t n16 = hdr.arena_bytes / 16;
     for (uint64_t i = (uint64_t)blockIdx.x * kECThreads + ctid; i < n16; i += (uint64_t)G * kECThreads)
       nz[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -582,7 +605,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   const unsigned char* ring = smem + hdr.ring_off + (size_t)warp * slots * kUnitBytes;
   int slot = 0;
   unsigned fph = 0u;
-  const uint32_t lanew = BITS <= 3 ? (uint32_t)lane * 4u : (uint32_t)lane * 4u * 0x10001u;
+  const uint32_t lanew =
+      BITS <= 3 ? (uint32_t)lane * 4u | (ABS ? 0x10000u : 0u) : (uint32_t)lane * 4u * 0x10001u;
   const int src = (lane & ~3) | ((t + 3) & 3);
 
   int done_upto = -1;  // newest stage known complete on every CTA (same in all consumer threads)
@@ -590,7 +614,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
   for (int si = 0, buf = 0; si < hdr.n_stages; ++si, buf = buf == 2 ? 0 : buf + 1) {
     bool ok = true;  // this warp's copies landed
     EStage st = s_st[buf];
-    if (st.dep >= 0) st.x = reinterpret_cast<const void*>(hdr.arena[buf_y] + reinterpret_cast<uint64_t>(st.x));
+    if (st.dep >= 0) st.x = reinterpret_cast<const void*>(arena_y + reinterpret_cast<uint64_t>(st.x));
     const EOp* cops = s_ops[buf];
     const int nbuf = buf == 2 ? 0 : buf + 1;
     etrace(si, 0);
@@ -702,8 +726,8 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
           }
           slot = slot2 + 1 == slots ? 0 : slot2 + 1;
           fph = slot2 + 1 == slots ? fph2 ^ 1u : fph2;
-          decode_unit<BITS, S>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
-          decode_unit<BITS, S>(lut, lanew, zq, cb2, prevg, prevq, t, src, zb + zu * (u * 32 + 32), zu * 16, accB);
+          decode_unit<BITS, S, ABS>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
+          decode_unit<BITS, S, ABS>(lut, lanew, zq, cb2, prevg, prevq, t, src, zb + zu * (u * 32 + 32), zu * 16, accB);
           u += 2;
           idx += 2;
         } else {
@@ -719,7 +743,7 @@ __global__ void __launch_bounds__(kEThreads, 1) tcq_engine_kernel(const EHeader*
           if (lane == 0) mbar_arrive(&s_empty[warp][slot]);
           slot = slot2;
           fph = fph2;
-          decode_unit<BITS, S>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
+          decode_unit<BITS, S, ABS>(lut, lanew, zq, ca, prevg, prevq, t, src, zb + zu * (u * 32), zu * 16, accA);
           u += 1;
           idx += 1;
         }
@@ -800,9 +824,9 @@ int sm_count_e() {
 
 inline uint32_t al128(uint64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); }
 
-template <int BITS, int S>
+template <int BITS, int S, bool ABS>
 tp_status launch_engine_t(const EHeader& h, const void* image_dev, unsigned* counters, cudaStream_t st) {
-  auto kern = tcq_engine_kernel<BITS, S>;
+  auto kern = tcq_engine_kernel<BITS, S, ABS>;
   static int smem_set[64] = {0};
   if (tp_status s = ensure_smem(kern, h.smem, smem_set, "cudaFuncSetAttribute(engine)")) return s;
   cudaFuncAttributes fa{};
@@ -828,13 +852,43 @@ tp_status launch_engine_t(const EHeader& h, const void* image_dev, unsigned* cou
   return check_launch("tcq_engine_kernel");
 }
 
+template <int BITS, bool ABS>
+tp_status launch_engine_a(const EHeader& h, const void* img, unsigned* c, cudaStream_t st) {
+  switch (h.n_states) {
+    case 4: return launch_engine_t<BITS, 4, ABS>(h, img, c, st);
+    case 8: return launch_engine_t<BITS, 8, ABS>(h, img, c, st);
+    case 16: return launch_engine_t<BITS, 16, ABS>(h, img, c, st);
+    default: return launch_engine_t<BITS, 64, ABS>(h, img, c, st);
+  }
+}
 template <int BITS>
 tp_status launch_engine_s(const EHeader& h, const void* img, unsigned* c, cudaStream_t st) {
-  switch (h.n_states) {
-    case 4: return launch_engine_t<BITS, 4>(h, img, c, st);
-    case 8: return launch_engine_t<BITS, 8>(h, img, c, st);
-    case 16: return launch_engine_t<BITS, 16>(h, img, c, st);
-    default: return launch_engine_t<BITS, 64>(h, img, c, st);
+  if (BITS <= 3 && h.lut_abs) return launch_engine_a<BITS, true>(h, img, c, st);
+  return launch_engine_a<BITS, false>(h, img, c, st);
+}
+
+// static shared memory of the kernel that will run a program
+template <int BITS, bool ABS>
+size_t engine_static_smem_t(int n_states) {
+  cudaFuncAttributes fa{};
+  cudaError_t e;
+  switch (n_states) {
+    case 4: e = cudaFuncGetAttributes(&fa, tcq_engine_kernel<BITS, 4, ABS>); break;
+    case 8: e = cudaFuncGetAttributes(&fa, tcq_engine_kernel<BITS, 8, ABS>); break;
+    case 16: e = cudaFuncGetAttributes(&fa, tcq_engine_kernel<BITS, 16, ABS>); break;
+    default: e = cudaFuncGetAttributes(&fa, tcq_engine_kernel<BITS, 64, ABS>); break;
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return ~size_t(0);
+  }
+  return fa.sharedSizeBytes;
+}
+size_t engine_static_smem_abs(int bits, int n_states) {
+  switch (bits) {
+    case 1: return engine_static_smem_t<1, true>(n_states);
+    case 2: return engine_static_smem_t<2, true>(n_states);
+    default: return engine_static_smem_t<3, true>(n_states);
   }
 }
 
@@ -995,19 +1049,69 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
   const uint64_t scratch = (uint64_t)scratch_bytes;
   const uint64_t red = (uint64_t)max_tiles * kTileRows * 8 * 4;
   const uint64_t rowc = (uint64_t)max_tiles * kTileRows * 2 * 2;  // row scales + biases
-  const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red) + al128(rowc);
-  const uint64_t budget = 227u * 1024u - kEStaticSmem;
   const uint64_t unit = 512u * bits;
-  if (fixed + kEWarps * 2 * unit > budget)
-    return fail(TP_ERR_UNSUPPORTED, "engine: activations (%lld halves, B=%d) do not fit shared memory",
-                (long long)(zrows_q * 8), B);
-  hh.slots = static_cast<int32_t>(std::min<uint64_t>(kEMaxSlots, (budget - fixed) / (kEWarps * unit)));
-  hh.ring_off = lut;
-  hh.z_off = al128(hh.ring_off + (uint64_t)kEWarps * hh.slots * unit);
-  hh.scratch_off = al128(hh.z_off + zbytes);
-  hh.red_off = al128(hh.scratch_off + scratch);
-  hh.sc_off = al128(hh.red_off + red);
-  hh.smem = al128(hh.sc_off + rowc);
+  bool placed = false;
+  // bits <= 3: try the layout with the pair table at shared-window address
+  // 0x10000 (the weight ring and the other buffers around it)
+  const char* no_abs = getenv("TP_ENGINE_NO_ABS");
+  if (bits <= 3 && !(no_abs && no_abs[0] == '1')) {
+    int dev = 0, reserved = 0;
+    const size_t st_smem = engine_static_smem_abs(bits, n_states);
+    if (st_smem != ~size_t(0) && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess &&
+        st_smem <= kEStaticSmem) {
+      const uint64_t base = (reserved + st_smem + 127) / 128 * 128;  // dynamic area, 128-byte aligned
+      const uint64_t dyn_max = 227u * 1024u - st_smem;
+      if (base < 0x10000u && 0x10000u - base + lut <= dyn_max) {
+        const uint64_t front = 0x10000u - base, back0 = front + lut;
+        for (int slots = kEMaxSlots; slots >= 2 && !placed; --slots) {
+          // first fit, largest first: ring, scratch, zs, red, rowc -> front or back
+          struct Item { uint64_t bytes; uint32_t* off; } items[5] = {
+              {(uint64_t)kEWarps * slots * unit, &hh.ring_off}, {scratch, &hh.scratch_off}, {zbytes, &hh.z_off},
+              {red, &hh.red_off}, {rowc, &hh.sc_off}};
+          uint64_t f = 0, b = back0;
+          bool ok = true;
+          for (auto& it : items) {
+            const uint64_t sz = al128(it.bytes);
+            if (f + sz <= front) {
+              *it.off = static_cast<uint32_t>(f);
+              f += sz;
+            } else if (b + sz <= dyn_max) {
+              *it.off = static_cast<uint32_t>(b);
+              b += sz;
+            } else {
+              ok = false;
+              break;
+            }
+          }
+          if (ok) {
+            placed = true;
+            hh.slots = slots;
+            hh.lut_off = static_cast<uint32_t>(front);
+            hh.lut_abs = 1;
+            hh.dyn_base = static_cast<uint32_t>(base);
+            hh.smem = static_cast<uint32_t>(al128(b));
+          }
+        }
+      }
+    }
+  }
+  if (!placed) {
+    const uint64_t fixed = lut + al128(zbytes) + al128(scratch) + al128(red) + al128(rowc);
+    const uint64_t budget = 227u * 1024u - kEStaticSmem;
+    if (fixed + kEWarps * 2 * unit > budget)
+      return fail(TP_ERR_UNSUPPORTED, "engine: activations (%lld halves, B=%d) do not fit shared memory",
+                  (long long)(zrows_q * 8), B);
+    hh.slots = static_cast<int32_t>(std::min<uint64_t>(kEMaxSlots, (budget - fixed) / (kEWarps * unit)));
+    hh.lut_off = 0;
+    hh.lut_abs = 0;
+    hh.ring_off = lut;
+    hh.z_off = al128(hh.ring_off + (uint64_t)kEWarps * hh.slots * unit);
+    hh.scratch_off = al128(hh.z_off + zbytes);
+    hh.red_off = al128(hh.scratch_off + scratch);
+    hh.sc_off = al128(hh.red_off + red);
+    hh.smem = al128(hh.sc_off + rowc);
+  }
   *h = hh;
   return clear_ok();
 }
