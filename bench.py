@@ -45,7 +45,7 @@ LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down
 
 # DRAM bytes (read + write) of one engine launch / algorithmic bytes of the
 # step, from the ncu capture summarised under profiles/ (None: not captured)
-TRAFFIC_RATIO = 1.021
+TRAFFIC_RATIO = 1.025
 
 
 def linear_shapes(cfg: dict) -> list[tuple[str, int, int]]:
