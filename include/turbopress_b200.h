@@ -190,6 +190,18 @@ TP_API tp_status tp_tcq_gemv_noalloc(const void* x, int x_dtype, const uint16_t*
                                      int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block,
                                      int bits, int n_states, void* stream);
 
+/* Skinny GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulator)
+ * for batches of 16 and more: same arguments and result as tp_tcq_gemv.
+ * The weights are decoded into shared memory (fp16, UMMA operand layout) and
+ * multiplied with tcgen05.mma against the rotated activations; batches are
+ * processed 64 rows per pass.  Needs tp_gemm_tc_workspace_bytes(B, n, d)
+ * bytes of workspace (256-byte aligned; no zero-fill needed). */
+TP_API int64_t tp_gemm_tc_workspace_bytes(int64_t B, int64_t n, int64_t d);
+TP_API tp_status tp_tcq_gemm_tc(const void* x, int x_dtype, const uint16_t* rot_scale, const uint8_t* tcq_stream,
+                                const uint16_t* scales, const uint16_t* codebook, const uint16_t* bias, void* y,
+                                int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block, int bits,
+                                int n_states, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Persistent decode engine: a chain of packed linears in ONE launch.
  *

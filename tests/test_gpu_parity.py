@@ -381,3 +381,27 @@ def test_workspace_and_error_statuses():
     bad = args[:12] + (100,) + args[13:]
     assert L.tp_tcq_gemv(*bad, ws.data_ptr(), need, None) == _abi.TP_ERR_ARG  # block does not divide d
     torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 skinny GEMM (batch >= 16)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("bits,s,n,d,B", [(3, 64, 300, 1536, 16), (2, 16, 256, 1024, 48), (4, 64, 200, 768, 64),
+                                          (1, 8, 130, 512, 20), (3, 4, 1000, 700, 100), (3, 64, 4096, 2560, 32)])
+def test_gemm_tc_vs_oracle(bits, s, n, d, B):
+    from turbopress_b200 import _abi, PackedTCQLinear
+    p = O.random_payload(n, d, bits, s, seed=bits * 7 + n, bias=True)
+    m = PackedTCQLinear(to_dev(p), mode="cuda")
+    x = np.random.default_rng(B).standard_normal((B, d)).astype(np.float16)
+    xt = torch.from_numpy(x).to(DEV)
+    y = torch.empty(B, n, dtype=torch.float32, device=DEV)
+    lib = _abi.lib()
+    ws = torch.empty(lib.tp_gemm_tc_workspace_bytes(B, n, d), dtype=torch.uint8, device=DEV)
+    _abi.check(lib.tp_tcq_gemm_tc(xt.data_ptr(), _abi.TP_F16, m.rot_scale.data_ptr(), m.tcq_stream.data_ptr(),
+                                  m.scales.data_ptr(), m.codebook.data_ptr(), m.bias.data_ptr(), y.data_ptr(),
+                                  _abi.TP_F32, B, n, d, m.block, bits, s, ws.data_ptr(), ws.numel(),
+                                  torch.cuda.current_stream().cuda_stream), "gemm_tc")
+    assert rel_l2(y.cpu().numpy(), O.forward_fp32(p, x)) < REL_L2_TOL
+    # the module routes batches >= 16 here; below 16 it keeps the fused GEMV
+    y2 = m(xt.float()).cpu().numpy()
+    assert rel_l2(y2, O.forward_fp32(p, x)) < REL_L2_TOL

@@ -25,6 +25,8 @@ reference would first run them on the GPU.
 
 from __future__ import annotations
 
+import os
+
 import threading
 from typing import Any
 
@@ -48,6 +50,8 @@ __all__ = [
 ]
 
 MODES = ("cached", "tiled", "triton", "cuda")
+# batch size from which packed forwards use the tcgen05 skinny GEMM
+TC_MIN_BATCH = int(os.environ.get("TP_TC_MIN_BATCH", "16"))
 _PACKED_MODES = ("tiled", "triton", "cuda")
 
 # Rate-1/2 convolutional generators (octal) per state count
@@ -182,6 +186,9 @@ class _WorkspacePool:
 
 
 WORKSPACE = _WorkspacePool()
+# the tcgen05 path scribbles over its workspace: it must not share the GEMV's
+# (whose split-K counter block has to stay zero between calls)
+WORKSPACE_TC = _WorkspacePool()
 
 
 # ---------------------------------------------------------------------------
@@ -344,13 +351,17 @@ class PackedTCQLinear(nn.Module):
         st = _stream(flat)
         if self._native:
             _abi.require_cuda(self.tcq_stream)
-            ws_bytes = lib.tp_gemv_workspace_bytes(B, n, d, self.bits)
-            ws = WORKSPACE.get(x.device, ws_bytes)
-            _abi.check(lib.tp_tcq_gemv(
+            # batches of TC_MIN_BATCH and more: tcgen05 skinny GEMM; below: the fused GEMV
+            use_tc = B >= TC_MIN_BATCH
+            ws_bytes = (lib.tp_gemm_tc_workspace_bytes(B, n, d) if use_tc
+                        else lib.tp_gemv_workspace_bytes(B, n, d, self.bits))
+            ws = (WORKSPACE_TC if use_tc else WORKSPACE).get(x.device, ws_bytes)
+            fn = lib.tp_tcq_gemm_tc if use_tc else lib.tp_tcq_gemv
+            _abi.check(fn(
                 flat.data_ptr(), _abi.dtype_code(flat.dtype), self.rot_scale.data_ptr(), self.tcq_stream.data_ptr(),
                 self.scales.data_ptr(), self.codebook.data_ptr(), _abi.ptr(self.bias), y.data_ptr(),
                 _abi.dtype_code(y.dtype), B, n, d, self.block, self.bits, self.n_states, ws.data_ptr(), ws.numel(),
-                st), "tcq_gemv")
+                st), "tcq_gemm_tc" if use_tc else "tcq_gemv")
         else:
             z = rotate(flat, self.rot_scale, self.block, out_dtype=torch.float32)
             mem = None if self.member_packed is None else self.member_packed.contiguous()
