@@ -402,6 +402,6 @@ def test_gemm_tc_vs_oracle(bits, s, n, d, B):
                                   _abi.TP_F32, B, n, d, m.block, bits, s, ws.data_ptr(), ws.numel(),
                                   torch.cuda.current_stream().cuda_stream), "gemm_tc")
     assert rel_l2(y.cpu().numpy(), O.forward_fp32(p, x)) < REL_L2_TOL
-    # the module routes batches >= 16 here; below 16 it keeps the fused GEMV
+    # the module routes large batches here (TC_MIN_BATCH); smaller ones keep the fused GEMV
     y2 = m(xt.float()).cpu().numpy()
     assert rel_l2(y2, O.forward_fp32(p, x)) < REL_L2_TOL

@@ -21,11 +21,19 @@ using namespace tp;
 namespace {
 
 constexpr int kUWarps = 8;               // decode warps (one row tile each)
-constexpr int kUThreads = kUWarps * 32;
-constexpr int kUMaxN = 64;               // batch rows per launch
+constexpr int kUDecThreads = kUWarps * 32;
+constexpr int kUThreads = kUDecThreads + 32;  // + one MMA-issue warp
+constexpr int kUMaxN = 64;               // batch rows per launch (32 for 4-bit weights)
 constexpr uint32_t kATile = 128 * 128 * 2;   // one half unit of A: 32 KB
 constexpr uint32_t kCoreK = 128;             // bytes between K-adjacent core matrices
 constexpr uint32_t kCoreRows = 16 * 128;     // bytes between 8-row groups (16 core columns)
+
+// weight units in flight per decode warp (bulk-copy ring); 4-bit weights use
+// register prefetch (their 128 KB pair table leaves no room for a ring)
+template <int BITS>
+struct UDepth {
+  static constexpr int kDepth = BITS <= 3 ? 4 : 0;
+};
 
 struct UArgs {
   const uint4* stream;
@@ -34,7 +42,7 @@ struct UArgs {
   const __half* z;     // [NB][d_pad] permuted fp16 (rows >= B zero)
   float* y32;          // [B][n] fp32, zero before the launch
   int B, NB, n, d_pad, units_k, row_tiles, ksplit;
-  uint32_t lut_off, a_off, b_off, bar_off, smem;
+  uint32_t lut_off, a_off, b_off, w_off, bar_off, smem;
 };
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
@@ -112,12 +120,20 @@ __global__ void __launch_bounds__(kUThreads, 1) tcq_umma_kernel(UArgs a) {
   const bool have_rows = rt < a.row_tiles;
   const uint32_t ncols = a.NB <= 32 ? 32u : 64u;
 
+  constexpr int D = UDepth<BITS>::kDepth;
+  constexpr unsigned kUB = 512u * BITS;  // bytes of one unit
+  // bars: [0,2) A buffer free (tcgen05.commit), [2,4) A buffer ready (every
+  // decode thread arrives), then the weight-ring slots [kUWarps][D]
+  uint64_t* fullb = bars + 4;
   if (tid == 0) {
     s_bad = 0;
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
-    fence_mbar_init();
+    mbar_init(&bars[2], kUDecThreads);
+    mbar_init(&bars[3], kUDecThreads);
   }
+  if (D > 0 && tid < kUWarps * D) mbar_init(&fullb[tid], 1);
+  fence_mbar_init();
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"(ncols)
@@ -125,7 +141,7 @@ __global__ void __launch_bounds__(kUThreads, 1) tcq_umma_kernel(UArgs a) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   const uint32_t cbv = lane < (1 << (BITS + 1)) ? a.codebook[lane] : 0u;
-  build_lut<BITS>(lut, cbv, warp, lane, kUWarps);
+  build_lut<BITS>(lut, cbv, warp, lane, kUWarps + 1);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -134,80 +150,121 @@ __global__ void __launch_bounds__(kUThreads, 1) tcq_umma_kernel(UArgs a) {
   const int src = (lane & ~3) | ((t + 3) & 3);
   const uint32_t idesc = (1u << 4) | ((uint32_t)(a.NB >> 3) << 17) | ((128u >> 4) << 24);
 
-  // halo for the first unit of the range (from the previous unit of the row tile)
-  uint32_t prevg = 0u, prevq = 0u;
-  if (have_rows && u0 > 0) {
-    const uint4 pv = ldg_stream(a.stream + (((int64_t)rt * a.units_k + u0 - 1) * 32 + lane) * BITS);
-    prevg = pv.z;
-    prevq = pv.w;
-  }
-  uint4 cur[BITS], nxt[BITS];
-  if (have_rows && u0 < u1) {
-#pragma unroll
-    for (int k = 0; k < BITS; ++k) cur[k] = ldg_stream(a.stream + (((int64_t)rt * a.units_k + u0) * 32 + lane) * BITS + k);
-  }
   const int steps = 2 * (u1 - u0);
-  for (int h = 0; h < steps; ++h) {
-    const int buf = h & 1, u = u0 + (h >> 1), cgi = h & 1;
-    unsigned char* A = smem + a.a_off + buf * kATile;
-    unsigned char* Bt = smem + a.b_off + buf * (uint32_t)(a.NB * 256);
-    // the buffer is free once the MMAs of step h - 2 completed
-    if (h >= 2 && !mbar_wait(&bars[buf], (unsigned)(((h - 2) >> 1) & 1))) s_bad = 1;
-    // activations: rows b < NB, core columns of this half unit (16 x 16 B per row)
-    for (int i = tid; i < a.NB * 16; i += kUThreads) {
-      const int b = i >> 4, kc = i & 15;
-      const __half* srcp = a.z + (size_t)b * a.d_pad + (size_t)(u * 32 + cgi * 16 + kc) * 8;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Bt + (b >> 3) * kCoreRows +
-                                                                             kc * kCoreK + (b & 7) * 16)),
-                   "l"(srcp)
-                   : "memory");
+  const uint32_t btile = (uint32_t)(a.NB * 256);
+  unsigned char* wring = smem + a.w_off + (uint32_t)(warp < kUWarps ? warp : 0) * (D > 0 ? D : 1) * kUB;
+  const uint4* wsrc = a.stream + ((int64_t)rt * a.units_k) * 32 * BITS;  // unit u at wsrc + u * 32 * BITS
+  if (D > 0) {
+    __syncthreads();  // ring barriers initialised
+    if (warp < kUWarps && have_rows && lane == 0)
+      for (int i = 0; i < D && u0 + i < u1; ++i)
+        bulk_load(wring + i * kUB, wsrc + (int64_t)(u0 + i) * 32 * BITS, kUB, &fullb[warp * D + i]);
+  }
+  if (warp < kUWarps) {
+    // ===================== decode warps =====================
+    // activations of step h (rows b < NB, the 16 core columns of its half
+    // unit) into activation buffer h % 3, one cp.async group per step
+    auto copy_z = [&](int h) {
+      const int u = u0 + (h >> 1), cgi = h & 1;
+      unsigned char* Bt = smem + a.b_off + (uint32_t)(h % 3) * btile;
+      for (int i = tid; i < a.NB * 16; i += kUDecThreads) {
+        const int b = i >> 4, kc = i & 15;
+        const __half* srcp = a.z + (size_t)b * a.d_pad + (size_t)(u * 32 + cgi * 16 + kc) * 8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Bt + (b >> 3) * kCoreRows +
+                                                                               kc * kCoreK + (b & 7) * 16)),
+                     "l"(srcp)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // halo for the first unit of the range (from the previous unit of the row tile)
+    uint32_t prevg = 0u, prevq = 0u;
+    if (have_rows && u0 > 0) {
+      const uint4 pv = ldg_stream(wsrc + ((int64_t)(u0 - 1) * 32 + lane) * BITS);
+      prevg = pv.z;
+      prevq = pv.w;
     }
-    if (have_rows) {
-      if (cgi == 0 && u + 1 < u1) {  // prefetch the next unit of this row tile
+    uint4 cur[BITS], nxt[BITS];
+    if (D == 0 && have_rows && u0 < u1) {
 #pragma unroll
-        for (int k = 0; k < BITS; ++k)
-          nxt[k] = ldg_stream(a.stream + (((int64_t)rt * a.units_k + u + 1) * 32 + lane) * BITS + k);
-      }
-      const uint32_t P0g = cur[0].x, P0q = cur[0].y, P1g = cur[0].z, P1q = cur[0].w;
-      const uint32_t Pg = cgi ? P1g : P0g, Pq = cgi ? P1q : P0q;
-      const uint32_t Hg = __shfl_sync(0xffffffffu, t == 3 ? (cgi ? P0g : prevg) : Pg, src);
-      const uint32_t Hq = __shfl_sync(0xffffffffu, t == 3 ? (cgi ? P0q : prevq) : Pq, src);
-      uint32_t Mg0 = 0u, Mq0 = 0u, Mg1 = 0u, Mq1 = 0u, Mg2 = 0u, Mq2 = 0u;
-      if (BITS >= 2) {
-        Mg0 = cgi ? cur[1].z : cur[1].x;
-        Mq0 = cgi ? cur[1].w : cur[1].y;
-      }
-      if (BITS >= 3) {
-        Mg1 = cgi ? cur[2].z : cur[2].x;
-        Mq1 = cgi ? cur[2].w : cur[2].y;
-      }
-      if (BITS >= 4) {
-        Mg2 = cgi ? cur[3].z : cur[3].x;
-        Mq2 = cgi ? cur[3].w : cur[3].y;
-      }
-      const int rg = warp * 16 + g;  // A rows of this lane: rg and rg + 8
-      unsigned char* rows_g = A + (rg >> 3) * kCoreRows + (rg & 7) * 16;
-      unsigned char* rows_q = A + ((rg + 8) >> 3) * kCoreRows + ((rg + 8) & 7) * 16;
-      decode_half_store<BITS, S>(lut, lanew, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, rows_g, rows_q, t);
-      if (cgi == 1) {
-        prevg = P1g;
-        prevq = P1q;
-        if (u + 1 < u1) {
+      for (int k = 0; k < BITS; ++k) cur[k] = ldg_stream(wsrc + ((int64_t)u0 * 32 + lane) * BITS + k);
+    }
+    if (steps > 0) copy_z(0);
+    for (int h = 0; h < steps; ++h) {
+      const int buf = h & 1, u = u0 + (h >> 1), cgi = h & 1;
+      unsigned char* A = smem + a.a_off + buf * kATile;
+      // A buffer h % 2 and activation buffer (h + 1) % 3 == (h - 2) % 3 are
+      // free once the MMAs of step h - 2 completed
+      if (h >= 2 && !mbar_wait(&bars[buf], (unsigned)(((h - 2) >> 1) & 1))) s_bad = 1;
+      if (h + 1 < steps) copy_z(h + 1);  // in flight while this step decodes
+      if (have_rows) {
+        if (D > 0 && cgi == 0) {
+          // this unit from its ring slot; refill the slot with unit u + D
+          const int i = u - u0, slot = i % (D > 0 ? D : 1);
+          if (!mbar_wait(&fullb[warp * D + slot], (unsigned)((i / (D > 0 ? D : 1)) & 1))) s_bad = 1;
+          const uint4* su = reinterpret_cast<const uint4*>(wring + slot * kUB) + lane * BITS;
 #pragma unroll
-          for (int k = 0; k < BITS; ++k) cur[k] = nxt[k];
+          for (int k = 0; k < BITS; ++k) cur[k] = su[k];
+          __syncwarp();
+          if (lane == 0 && u + D < u1) {
+            fence_proxy_async();
+            bulk_load(wring + slot * kUB, wsrc + (int64_t)(u + D) * 32 * BITS, kUB, &fullb[warp * D + slot]);
+          }
+        } else if (D == 0 && cgi == 0 && u + 1 < u1) {  // prefetch the next unit of this row tile
+#pragma unroll
+          for (int k = 0; k < BITS; ++k) nxt[k] = ldg_stream(wsrc + ((int64_t)(u + 1) * 32 + lane) * BITS + k);
+        }
+        const uint32_t P0g = cur[0].x, P0q = cur[0].y, P1g = cur[0].z, P1q = cur[0].w;
+        const uint32_t Pg = cgi ? P1g : P0g, Pq = cgi ? P1q : P0q;
+        const uint32_t Hg = __shfl_sync(0xffffffffu, t == 3 ? (cgi ? P0g : prevg) : Pg, src);
+        const uint32_t Hq = __shfl_sync(0xffffffffu, t == 3 ? (cgi ? P0q : prevq) : Pq, src);
+        uint32_t Mg0 = 0u, Mq0 = 0u, Mg1 = 0u, Mq1 = 0u, Mg2 = 0u, Mq2 = 0u;
+        if (BITS >= 2) {
+          Mg0 = cgi ? cur[1].z : cur[1].x;
+          Mq0 = cgi ? cur[1].w : cur[1].y;
+        }
+        if (BITS >= 3) {
+          Mg1 = cgi ? cur[2].z : cur[2].x;
+          Mq1 = cgi ? cur[2].w : cur[2].y;
+        }
+        if (BITS >= 4) {
+          Mg2 = cgi ? cur[3].z : cur[3].x;
+          Mq2 = cgi ? cur[3].w : cur[3].y;
+        }
+        const int rg = warp * 16 + g;  // A rows of this lane: rg and rg + 8
+        unsigned char* rows_g = A + (rg >> 3) * kCoreRows + (rg & 7) * 16;
+        unsigned char* rows_q = A + ((rg + 8) >> 3) * kCoreRows + ((rg + 8) & 7) * 16;
+        decode_half_store<BITS, S>(lut, lanew, Pg, Hg, Pq, Hq, Mg0, Mg1, Mg2, Mq0, Mq1, Mq2, rows_g, rows_q, t);
+        if (cgi == 1) {
+          prevg = P1g;
+          prevq = P1q;
+          if (D == 0 && u + 1 < u1) {
+#pragma unroll
+            for (int k = 0; k < BITS; ++k) cur[k] = nxt[k];
+          }
         }
       }
+      // this step's activations landed (the next step's group may still be in flight)
+      if (h + 1 < steps) asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else asm volatile("cp.async.wait_group 0;" ::: "memory");
+      fence_proxy_async();  // generic-proxy writes of A and B -> visible to the tensor core
+      mbar_arrive(&bars[2 + buf]);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    fence_proxy_async();  // generic-proxy writes of A and B -> visible to the tensor core
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
+  } else if (lane == 0) {
+    // ===================== MMA warp =====================
+    for (int h = 0; h < steps; ++h) {
+      const int buf = h & 1;
+      if (!mbar_wait(&bars[2 + buf], (unsigned)((h >> 1) & 1))) {
+        s_bad = 1;
+        break;
+      }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a0 = smem_u32(A), b0 = smem_u32(Bt);
+      const uint32_t a0 = smem_u32(smem + a.a_off + buf * kATile);
+      const uint32_t b0 = smem_u32(smem + a.b_off + (uint32_t)(h % 3) * btile);
 #pragma unroll
       for (int s = 0; s < 8; ++s)  // K = 16 per MMA: two core columns
-        umma_f16(tmem, umma_desc(a0 + s * 2 * kCoreK), umma_desc(b0 + s * 2 * kCoreK), idesc, (h > 0 || s > 0) ? 1u : 0u);
+        umma_f16(tmem, umma_desc(a0 + s * 2 * kCoreK), umma_desc(b0 + s * 2 * kCoreK), idesc,
+                 (h > 0 || s > 0) ? 1u : 0u);
       umma_commit(&bars[buf]);
     }
   }
@@ -319,12 +376,13 @@ extern "C" tp_status tp_tcq_gemm_tc(const void* x, int x_dtype, const uint16_t* 
   const int row_tiles = (int)(n_pad / kTileRows);
   const int m_tiles = (int)((n + 127) / 128);
   const int G = sm_count_u();
-  int ksplit = (G + m_tiles - 1) / m_tiles;
+  int ksplit = G / m_tiles;  // one CTA per SM: keep the grid within one wave
   if (ksplit > units_k) ksplit = units_k;
   if (ksplit < 1) ksplit = 1;
   const uint32_t lut = bits == 4 ? LutCfg<4>::kLutBytes : LutCfg<3>::kLutBytes;
-  for (int64_t b0 = 0; b0 < B; b0 += kUMaxN) {
-    const int nb = (int)(B - b0 < kUMaxN ? B - b0 : kUMaxN);
+  const int64_t max_n = bits == 4 ? 32 : kUMaxN;
+  for (int64_t b0 = 0; b0 < B; b0 += max_n) {
+    const int nb = (int)(B - b0 < max_n ? B - b0 : max_n);
     const int NB = (nb + 15) / 16 * 16;
     __half* z = static_cast<__half*>(workspace);
     float* y32 = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + pad_to((int64_t)NB * d_pad * 2, 256));
@@ -358,8 +416,10 @@ extern "C" tp_status tp_tcq_gemm_tc(const void* x, int x_dtype, const uint16_t* 
     a.lut_off = 0;
     a.a_off = lut;
     a.b_off = a.a_off + 2 * kATile;
-    a.bar_off = a.b_off + 2 * (uint32_t)(NB * 256);
-    a.smem = a.bar_off + 64;
+    a.w_off = a.b_off + 3 * (uint32_t)(NB * 256);
+    const uint32_t depth = bits <= 3 ? 4u : 0u;
+    a.bar_off = a.w_off + (uint32_t)kUWarps * depth * 512u * (uint32_t)bits;
+    a.smem = a.bar_off + 8u * (4u + (uint32_t)kUWarps * depth);
     tp_status s;
     switch (bits) {
       case 1: s = launch_umma_s<1>(a, m_tiles, n_states, st); break;
