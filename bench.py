@@ -640,7 +640,7 @@ def run_gemv(args) -> dict:
         us = e0.elapsed_time(e1) * 1e3 / args.steps / copies
         nbytes = gemv_bytes(n, d, args.bits, args.batch)
         res[shp] = {"us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1), "MB": round(nbytes / 1e6, 2),
-                    "copies": copies}
+                    "TFLOPs": round(2 * args.batch * n * d / us / 1e6, 2), "copies": copies}
         del mods, graph
         torch.cuda.empty_cache()
     return {"workload": "gemv", "bits": args.bits, "batch": args.batch, "shapes": res}
