@@ -39,7 +39,16 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-QWEN3_4B = dict(name="qwen3-4b", layers=36, hidden=2560, inter=9728, q_heads=32, kv_heads=8, head_dim=128)
+QWEN3_4B = dict(name="qwen3-4b", label="Qwen3-4B", layers=36, hidden=2560, inter=9728, q_heads=32, kv_heads=8,
+                head_dim=128)
+# the tensor-parallel configuration (2-bit, TP 1/2/4/8); not the contract line
+LLAMA3_70B = dict(name="llama3-70b", label="Llama-3-70B", layers=80, hidden=8192, inter=28672, q_heads=64,
+                  kv_heads=8, head_dim=128)
+MODELS = {"qwen3-4b": QWEN3_4B, "llama3-70b": LLAMA3_70B}
+
+
+def metric_name(cfg: dict, bits: int) -> str:
+    return f"TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s, {bits}-bit {cfg['label']} shape"
 LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 
 
@@ -300,7 +309,7 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
     per_gpu_bytes = step_bytes / world
     ach = per_gpu_bytes / (ms_kernel * 1e-3) / 1e9
     out = {
-        "metric": "TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s, 3-bit Qwen3-4B shape",
+        "metric": metric_name(cfg, bits),
         "value": round(step_bytes / (ms * 1e-3) / 1e9, 1),
         "unit": "GB/s",
         "n_gpus": world,
@@ -310,9 +319,9 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "u8 packed TCQ (3 bits/weight) -> fp16 activations, fp32 accumulate",
+        "dtype": f"u8 packed TCQ ({bits} bits/weight) -> fp16 activations, fp32 accumulate",
         "data": "synthetic: seeded random trellis streams + reference data-free codebook; x N(0,1) fp16",
-        "config": {"workload": f"qwen3-4b decoder linears, batch {B}, {bits}-bit packed TCQ, S=64",
+        "config": {"workload": f"{cfg['name']} decoder linears, batch {B}, {bits}-bit packed TCQ, S=64",
                    "path": f"tensor-parallel persistent engine over {world} GPUs (row-sharded linears, "
                            "outputs added into every rank's arena over NVLink peer memory), CUDA graph",
                    "layers": cfg["layers"], "linears_per_step": cfg["layers"] * len(LINEARS), "batch": B,
@@ -355,7 +364,7 @@ def run_gpu(args) -> dict | None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    cfg, bits, B = dict(QWEN3_4B), args.bits, args.batch
+    cfg, bits, B = dict(MODELS[args.model]), args.bits, args.batch
     if args.layers:
         cfg["layers"] = args.layers  # profiling of a small case only
     if world > 1:
@@ -534,7 +543,7 @@ def run_gpu(args) -> dict | None:
         launches = args.steps * n_gemv * launches_per_gemv
         path = "per-layer tp_tcq_gemv calls, CUDA graph"
     out = {
-        "metric": "TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s, 3-bit Qwen3-4B shape",
+        "metric": metric_name(cfg, bits),
         "value": round(value, 1),
         "unit": "GB/s",
         "n_gpus": world,
@@ -544,9 +553,9 @@ def run_gpu(args) -> dict | None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "u8 packed TCQ (3 bits/weight) -> fp16 activations, fp32 accumulate",
+        "dtype": f"u8 packed TCQ ({bits} bits/weight) -> fp16 activations, fp32 accumulate",
         "data": "synthetic: seeded random trellis streams + reference data-free codebook; x N(0,1) fp16",
-        "config": {"workload": f"qwen3-4b decoder linears, batch {B}, {bits}-bit packed TCQ, S=64",
+        "config": {"workload": f"{cfg['name']} decoder linears, batch {B}, {bits}-bit packed TCQ, S=64",
                    "path": path,
                    "layers": cfg["layers"], "linears_per_step": n_gemv, "batch": B, "bits": bits,
                    "weights_bytes_per_step": int(step_bytes),
@@ -650,7 +659,7 @@ def run_reference(args) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    cfg, bits = QWEN3_4B, args.bits
+    cfg, bits = dict(MODELS[args.model]), args.bits
     for i in range(args.warmup):
         cpu_baseline_sample(cfg, bits, [i], seed=args.seed)
     vals, tot_b, tot_t = [], 0, 0.0
@@ -663,12 +672,12 @@ def run_reference(args) -> dict | None:
     ms = tot_t / args.steps * 1e3
     return {
         "impl": "reference",
-        "metric": "TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s, 3-bit Qwen3-4B shape",
+        "metric": metric_name(cfg, bits),
         "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8 packed TCQ -> fp32 (reference CPU path)",
         "data": "synthetic: seeded random trellis streams + reference data-free codebook",
-        "config": {"workload": f"qwen3-4b decoder linears, batch 1, {bits}-bit packed TCQ, S=64",
+        "config": {"workload": f"{cfg['name']} decoder linears, batch 1, {bits}-bit packed TCQ, S=64",
                    "sample": "one linear per step, cycling q/k/v/o/gate/up/down"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": "oracle port of the reference tiled forward (unpack, window decode, fp16 "
@@ -687,6 +696,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-4b",
+                    help="decode workload: model shape (qwen3-4b is the contract line)")
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (default: the model's 36; "
                     "smaller values are for ncu captures, not bench lines)")
     ap.add_argument("--no-engine", action="store_true", help="decode workload: per-layer graph only")

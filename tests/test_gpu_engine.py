@@ -76,7 +76,8 @@ def test_engine_decoder_chain(bits, B):
         _check_ops(eng, payloads, inputs, {h: x}, outs)
 
 
-@pytest.mark.parametrize("n,d", [(4096, 2560), (8192, 512), (2560, 9728), (9728, 2560), (96, 200), (1024, 1)])
+@pytest.mark.parametrize("n,d", [(4096, 2560), (8192, 512), (2560, 9728), (9728, 2560), (96, 200), (1024, 1),
+                                 (256, 28672), (512, 8192), (300, 12288)])
 def test_engine_single_op_shapes(n, d):
     from turbopress_b200.engine import DecodeEngine
     p = O.random_payload(n, d, 3, 64, seed=n + d, bias=True)
@@ -140,3 +141,25 @@ def test_engine_rejects():
     p4 = O.random_payload(64, 256, 4, 64, seed=1)
     with pytest.raises(ValueError):
         DecodeEngine([m, _module(p4)])  # mixed bit widths
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_engine_wide_chain(B):
+    """Llama-70B widths (rows scaled down for the oracle): q/k/v and gate/up
+    read 8192-wide inputs with Hadamard block 8192, down a 28672-wide one
+    (block 4096); these blocks are transformed straight from global memory.
+    The 28672-wide activations fit shared memory at batch 1 only."""
+    from turbopress_b200.engine import DecodeEngine
+    h, inter = 8192, 28672
+    cb = np.sort(np.random.default_rng(5).standard_normal(8) * 1.2)
+    shapes = [(512, h, None), (128, h, None), (128, h, None), (h, 512, 0), (1024, h, 3), (1024, h, 3),
+              (512, inter, None)][:7 if B == 1 else 6]
+    payloads = [O.random_payload(n, d, 2, 64, seed=40 + i, codebook=cb) for i, (n, d, _) in enumerate(shapes)]
+    inputs = [dep for _, _, dep in shapes]
+    eng = DecodeEngine([_module(p) for p in payloads], inputs, batch=B)
+    rng = np.random.default_rng(6)
+    xs = {w: rng.standard_normal((B, w)).astype(np.float16) for w in ((h, inter) if B == 1 else (h,))}
+    outs = eng.run([torch.from_numpy(v).to(DEV) for v in xs.values()])
+    torch.cuda.synchronize()
+    eng.check()
+    _check_ops(eng, payloads, inputs, xs, outs)

@@ -76,6 +76,7 @@ struct alignas(16) EStage {
   int32_t rows_per_pass;       // batch rows of x staged per pass
   float norm;                  // 1/sqrt(block)
   uint32_t rs_off, work_off;   // in the scratch area: staged rot_scale rows, fp32 work row
+  int32_t direct, pad_s;       // 1: blocks go through the work row straight from global memory (no x / rot_scale staging)
 };
 
 struct alignas(16) EHeader {
@@ -282,8 +283,10 @@ __device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* z
   const uint16_t* rs = reinterpret_cast<const uint16_t*>(scr + st.rs_off);
   for (int b0 = 0; b0 < B; b0 += st.rows_per_pass) {
     const int rows = B - b0 < st.rows_per_pass ? B - b0 : st.rows_per_pass;
-    stage_inputs(st, cops, b0, rows, b0 == 0, scr, ctid);
-    csync();
+    if (!st.direct) {
+      stage_inputs(st, cops, b0, rows, b0 == 0, scr, ctid);
+      csync();
+    }
     if (b0 == 0) etrace(si, 5);
     if (st.block >= 32 && st.block <= 1024) {
       // warp jobs (op j, row rr, block kb), kb fastest
@@ -326,8 +329,14 @@ __device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* z
         for (int rr = 0; rr < rows; ++rr)
           for (int kb = 0; kb < nblk; ++kb) {
             const int c0 = kb * st.block;
-            for (int c = ctid; c < st.block; c += kECThreads)
-              work[c] = xs_at(scr, dt, rr * st.d + c0 + c) * h2f_bits(rs[j * st.d + c0 + c]);
+            if (st.direct) {
+              // wide inputs: one block of x * rot_scale read from global memory (L2)
+              for (int c = ctid; c < st.block; c += kECThreads)
+                work[c] = load_x(st, (int64_t)(b0 + rr) * st.d + c0 + c) * h2f_bits(cops[j].rot_scale[c0 + c]);
+            } else {
+              for (int c = ctid; c < st.block; c += kECThreads)
+                work[c] = xs_at(scr, dt, rr * st.d + c0 + c) * h2f_bits(rs[j * st.d + c0 + c]);
+            }
             csync();
             int b_start = 0;
             if (st.block > 1024) {
@@ -956,9 +965,10 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
     if (!st.empty()) {
       const EStage& c = st.back();
       const tp_engine_op& f = ops[c.first_op];
+      // activations (+ staged rot_scale rows, except for direct stages)
+      const int64_t row_bytes = B * d_pad * 2 + (c.direct ? 0 : s.d * 2);
       join = f.x == s.x && f.x_dtype == s.x_dtype && f.dep == s.dep && f.d == s.d && f.block == s.block &&
-             c.n_ops < kEMaxStageOps &&
-             (int64_t)(c.n_ops + 1) * (B * d_pad * 2 + s.d * 2) <= kEZStageBytes;  // activations + rot_scale rows
+             c.n_ops < kEMaxStageOps && (int64_t)(c.n_ops + 1) * row_bytes <= kEZStageBytes;
     }
     if (!join) {
       EStage e{};
@@ -976,6 +986,10 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
       e.norm = static_cast<float>(1.0 / __builtin_sqrt(static_cast<double>(s.block)));
       // raw cp.async staging: 16-byte aligned rows of x and of rot_scale
       e.vec = (s.d % 8 == 0 && aligned(s.x, 16)) ? 1 : 0;
+      // blocks above 1024 are transformed one at a time through the fp32 work
+      // row anyway; reading them straight from global memory keeps wide
+      // inputs (d up to 32K) within shared memory
+      e.direct = s.block > 1024 ? 1 : 0;
       st.push_back(e);
     }
     stage_of[i] = static_cast<int>(st.size()) - 1;
@@ -1012,9 +1026,10 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
     const int64_t jobs = (int64_t)c.n_ops * B;
     // scratch: staged x rows (raw dtype, or fp32), rot_scale rows, fp32 work row
     const int64_t xes = c.vec && c.x_dtype != TP_F32 ? 2 : 4;
-    c.rows_per_pass = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(B, kEXStageBytes / (c.d * xes))));
-    c.rs_off = static_cast<uint32_t>(pad_to((int64_t)c.rows_per_pass * c.d * xes, 16));
-    const int64_t rs_end = c.rs_off + pad_to((int64_t)c.n_ops * c.d * 2, 16);
+    c.rows_per_pass = c.direct ? B
+                                : static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(B, kEXStageBytes / (c.d * xes))));
+    c.rs_off = c.direct ? 0 : static_cast<uint32_t>(pad_to((int64_t)c.rows_per_pass * c.d * xes, 16));
+    const int64_t rs_end = c.direct ? 0 : c.rs_off + pad_to((int64_t)c.n_ops * c.d * 2, 16);
     // fp32 work row for blocks not done as one warp job
     c.work_off = static_cast<uint32_t>(rs_end);
     const int64_t work = (c.block > 1024 || c.block < 32) ? (int64_t)c.block * 4 : 0;
