@@ -76,7 +76,8 @@ struct alignas(16) EStage {
   int32_t rows_per_pass;       // batch rows of x staged per pass
   float norm;                  // 1/sqrt(block)
   uint32_t rs_off, work_off;   // in the scratch area: staged rot_scale rows, fp32 work row
-  int32_t direct, pad_s;       // 1: blocks go through the work row straight from global memory (no x / rot_scale staging)
+  int32_t direct;              // 1: blocks above 1024, read straight from global memory (no x / rot_scale staging)
+  int32_t work_blocks;         // direct stages: Hadamard blocks per pass through the fp32 work area
 };
 
 struct alignas(16) EHeader {
@@ -269,6 +270,32 @@ __device__ void fwht_consumers(float* s, int count, int b_start, int lg, int cti
   }
 }
 
+// R-point transform of the values at one position of R consecutive 512-wide
+// chunks (stride 512 in the work area; the chunks are already transformed),
+// scaled and written as fp16 activations of absolute columns cc0 + 512 e.
+template <int R>
+__device__ __forceinline__ void chunk_combine(const float* w, __half* zrow, int cc0, float norm) {
+  float v[R];
+#pragma unroll
+  for (int e = 0; e < R; ++e) v[e] = w[e * 512];
+#pragma unroll
+  for (int h = 1; h < R; h <<= 1) {
+#pragma unroll
+    for (int e = 0; e < R; ++e) {
+      if (!(e & h)) {
+        const float a = v[e], b = v[e + h];
+        v[e] = a + b;
+        v[e + h] = a - b;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < R; ++e) {
+    const int cc = cc0 + e * 512;
+    zrow[(cc & ~31) + zperm_pos(cc & 31)] = __float2half_rn(v[e] * norm);
+  }
+}
+
 // x -> fp16 rotated activations of every (op j, batch row b) job of the
 // stage; the job's row lives at zs + (j * B + b) * d_pad.  Blocks of
 // 32..1024 are one warp job each (registers + shuffles); larger blocks go
@@ -320,6 +347,45 @@ __device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* z
           }
         }
       }
+    } else if (st.direct) {
+      // blocks of 2048..8192, work_blocks at a time: (A) every warp transforms
+      // 512-wide chunks of x * rot_scale, loaded straight from global memory
+      // (L2), in registers into the fp32 work area; (B) every consumer thread
+      // combines the block/512 chunk values at one position and writes them.
+      float* work = reinterpret_cast<float*>(scr + st.work_off);
+      const int R = st.block >> 9;
+      for (int j = 0; j < st.n_ops; ++j) {
+        const uint16_t* rsg = cops[j].rot_scale;
+        for (int rr = 0; rr < rows; ++rr) {
+          __half* zrow = zs + (size_t)(j * B + b0 + rr) * st.d_pad;
+          const int64_t xrow = (int64_t)(b0 + rr) * st.d;
+          for (int kb0 = 0; kb0 < nblk; kb0 += st.work_blocks) {
+            const int nb = nblk - kb0 < st.work_blocks ? nblk - kb0 : st.work_blocks;
+            const int c0 = kb0 * st.block;
+            for (int ch = warp; ch < nb * R; ch += kEWarps) {
+              const int cb = c0 + ch * 512;
+              float v[16];
+#pragma unroll
+              for (int r = 0; r < 16; ++r) v[r] = load_x(st, xrow + cb + lane + 32 * r);
+#pragma unroll
+              for (int r = 0; r < 16; ++r) v[r] *= h2f_bits(rsg[cb + lane + 32 * r]);
+              warp_fwht_regs<16>(v, lane);
+#pragma unroll
+              for (int r = 0; r < 16; ++r) work[ch * 512 + lane + 32 * r] = v[r];
+            }
+            csync();
+            for (int g = ctid; g < nb * 512; g += kECThreads) {
+              const int b = g >> 9, p = g & 511;
+              const float* w = work + b * st.block + p;
+              const int cc0 = c0 + b * st.block + p;
+              if (R == 4) chunk_combine<4>(w, zrow, cc0, st.norm);
+              else if (R == 8) chunk_combine<8>(w, zrow, cc0, st.norm);
+              else chunk_combine<16>(w, zrow, cc0, st.norm);
+            }
+            csync();
+          }
+        }
+      }
     } else {
       // one Hadamard block at a time through the fp32 work row: blocks above
       // 1024 as 512-wide warp transforms plus consumer-wide passes over the
@@ -329,14 +395,8 @@ __device__ void rotate_stage(const EStage& st, const EOp* cops, int B, __half* z
         for (int rr = 0; rr < rows; ++rr)
           for (int kb = 0; kb < nblk; ++kb) {
             const int c0 = kb * st.block;
-            if (st.direct) {
-              // wide inputs: one block of x * rot_scale read from global memory (L2)
-              for (int c = ctid; c < st.block; c += kECThreads)
-                work[c] = load_x(st, (int64_t)(b0 + rr) * st.d + c0 + c) * h2f_bits(cops[j].rot_scale[c0 + c]);
-            } else {
-              for (int c = ctid; c < st.block; c += kECThreads)
-                work[c] = xs_at(scr, dt, rr * st.d + c0 + c) * h2f_bits(rs[j * st.d + c0 + c]);
-            }
+            for (int c = ctid; c < st.block; c += kECThreads)
+              work[c] = xs_at(scr, dt, rr * st.d + c0 + c) * h2f_bits(rs[j * st.d + c0 + c]);
             csync();
             int b_start = 0;
             if (st.block > 1024) {
@@ -1032,7 +1092,10 @@ tp_status build_impl(const tp_engine_op* ops, const int64_t* row0, const int64_t
     const int64_t rs_end = c.direct ? 0 : c.rs_off + pad_to((int64_t)c.n_ops * c.d * 2, 16);
     // fp32 work row for blocks not done as one warp job
     c.work_off = static_cast<uint32_t>(rs_end);
-    const int64_t work = (c.block > 1024 || c.block < 32) ? (int64_t)c.block * 4 : 0;
+    // direct stages: as many whole blocks per pass as fit 32 KB (8192 floats)
+    c.work_blocks = c.direct ? static_cast<int32_t>(std::max(1, std::min(c.d / c.block, 8192 / c.block))) : 0;
+    const int64_t work = c.direct ? (int64_t)c.work_blocks * c.block * 4
+                                  : (c.block > 1024 || c.block < 32) ? (int64_t)c.block * 4 : 0;
     scratch_bytes = std::max<int64_t>(scratch_bytes, rs_end + work);
     zrows_q = std::max<int64_t>(zrows_q, jobs * c.d_pad / 8);
     const int64_t per_cta = (kEWarps * (int64_t)c.total_units + V - 1) / V;
