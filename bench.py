@@ -20,6 +20,14 @@ from HBM.
              graph replay)
   --impl reference : the reference path's CPU restatement (oracle port) on
              the host cores, on bounded samples of the same workload.
+
+Under torchrun (N > 1) every rank first runs the tensor-parallel engine (each
+linear row-sharded over the N GPUs, outputs exchanged over NVLink inside the
+kernel) and reports it under "tp"; the line's value then comes from N
+replicas, each GPU decoding its own batch-1 stream with the whole model
+(scaling "weak"), which is how a 4B model is served on N GPUs.
+--parallel tp makes the tensor-parallel step the line itself (the
+Llama-3-70B-shaped configuration: --model llama3-70b --bits 2).
 """
 
 from __future__ import annotations
@@ -302,8 +310,9 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e, ms_kernel = (float(v) for v in t)
     eng.close()
+    del eng
+    torch.cuda.empty_cache()
     if rank != 0:
-        dist.destroy_process_group()
         return None
     peak, peak_src = peaks_hbm()
     per_gpu_bytes = step_bytes / world
@@ -341,7 +350,6 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
                      "kernel_ms": round(ms_kernel, 4), "peak_source": peak_src},
         "clocks": clk.summary(),
     }
-    dist.destroy_process_group()
     return out
 
 
@@ -367,8 +375,14 @@ def run_gpu(args) -> dict | None:
     cfg, bits, B = dict(MODELS[args.model]), args.bits, args.batch
     if args.layers:
         cfg["layers"] = args.layers  # profiling of a small case only
+    tp_line = None
     if world > 1:
-        return run_tp(args, cfg, rank, world, local, dev, dist)
+        # tensor parallel: one model split over the ranks (latency of one stream)
+        tp_line = run_tp(args, cfg, rank, world, local, dev, dist)
+        if args.parallel == "tp":
+            dist.destroy_process_group()
+            return tp_line
+        # replicas: every rank decodes its own batch-1 stream with the whole model
     mods = build_model(cfg, bits, dev, seed=args.seed)
     step_bytes = sum(gemv_bytes(n, d, bits, B) for _ in range(cfg["layers"]) for _, d, n in linear_shapes(cfg))
     n_gemv = cfg["layers"] * len(LINEARS)
@@ -576,7 +590,12 @@ def run_gpu(args) -> dict | None:
                          "value": round(world * step_bytes / (ms_eng * 1e-3) / 1e9, 1),
                          "tok_s": round(world * B * 1000.0 / ms_eng, 1),
                          "e2e_tok_s": round(world * B * 1000.0 / ms_eng_e2e, 1)}
-    if not args.no_cpu_baseline:
+    if tp_line is not None:
+        out["tp"] = {"parallelism": f"tp{world}", "ms_per_step": tp_line["ms_per_step"], "tok_s": tp_line["tok_s"],
+                     "value": tp_line["value"], "unit": "GB/s", "e2e_tok_s": tp_line["e2e"]["tok_s"],
+                     "kernel_ms": tp_line["roofline"]["kernel_ms"], "roofline_frac": tp_line["roofline"]["frac"],
+                     "path": tp_line["config"]["path"]}
+    if not args.no_cpu_baseline and world == 1:
         gbs, nbytes, secs = cpu_baseline_sample(cfg, bits, list(range(7)), seed=args.seed)
         out["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
                                "sample": f"oracle forward of one decoder layer (7 linears, {nbytes / 1e6:.1f} MB "
@@ -655,6 +674,43 @@ def run_gemv(args) -> dict:
     return {"workload": "gemv", "bits": args.bits, "batch": args.batch, "shapes": res}
 
 
+def run_lmhead(args) -> dict:
+    """Greedy LM head (fp16 vocabulary GEMV + argmax), Qwen3 vocabulary x the
+    model's hidden size: GB/s of weight bytes over the kernel's event time."""
+    import torch
+
+    from turbopress_b200.lm_head import GreedyLMHead
+
+    cfg = MODELS[args.model]
+    V, h, B = 151936, cfg["hidden"], args.batch
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    w = (torch.randn(V, h, generator=g, device=dev) * 0.02).half()  # 0.78 GB at h = 2560: larger than L2
+    x = torch.randn(B, h, generator=g, device=dev).half()
+    head = GreedyLMHead(w)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            head(x)
+        stream.synchronize()
+        with ClockSampler(0) as clk:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.steps):
+                tok, _ = head(x)
+            b.record(stream)
+            b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    nbytes = V * h * 2 + B * h * 2 + B * 12
+    peak, peak_src = peaks_hbm()
+    ach = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "lmhead", "vocab": V, "hidden": h, "batch": B, "us": round(ms * 1e3, 2),
+            "gbs": round(ach, 1), "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                                               "unit": "GB/s", "frac": round(ach / peak, 4),
+                                               "peak_source": peak_src},
+            "token": tok.cpu().tolist(), "clocks": clk.summary()}
+
+
 def run_reference(args) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -698,16 +754,22 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-4b",
                     help="decode workload: model shape (qwen3-4b is the contract line)")
+    ap.add_argument("--parallel", choices=["replicas", "tp"], default="replicas",
+                    help="N > 1: the JSON line's value from N independent batch-1 streams (replicas, with the "
+                         "tensor-parallel step reported under 'tp') or from the tensor-parallel step itself")
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (default: the model's 36; "
                     "smaller values are for ncu captures, not bench lines)")
     ap.add_argument("--no-engine", action="store_true", help="decode workload: per-layer graph only")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "gemv", "lmhead"], default="decode",
                     help="decode: the contract line (Qwen3-4B decode step); gemv: standalone GEMV table")
     ap.add_argument("--shapes", default="14336x4096,4096x14336,4096x4096,1024x4096",
                     help="gemv workload: comma-separated NxD (out x in) shapes")
     ap.add_argument("--copies", type=int, default=16, help="gemv workload: distinct weight sets per shape")
     ap.add_argument("--once", action="store_true", help="gemv workload: one call per shape (profiling)")
     args = ap.parse_args()
+    if args.workload == "lmhead" and args.impl != "reference":
+        print(json.dumps(run_lmhead(args)), flush=True)
+        return
     if args.workload == "gemv" and args.impl != "reference":
         print(json.dumps(run_gemv(args)), flush=True)
         return

@@ -202,6 +202,22 @@ TP_API tp_status tp_tcq_gemm_tc(const void* x, int x_dtype, const uint16_t* rot_
                                 int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block, int bits,
                                 int n_states, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Greedy LM head: idx[b] = argmax_v (x[b] . w[v]) over a fp16 weight matrix
+ * w [V][h] (row-major, 16-byte aligned, h a multiple of 8) and fp16 input
+ * x [B][h] (16-byte aligned), 1 <= B <= 8, B*h <= 25600; fp32 accumulation;
+ * the first index wins among equal logits (NaN counts as largest).  val[b]
+ * (NULL to skip) receives the winning logit; logits (fp32 [B][V], NULL to
+ * skip) all of them.  One HBM-bound pass over w; the logits are not needed
+ * in memory.  Needs tp_lm_head_workspace_bytes(B) bytes of workspace,
+ * zero-filled once (every call leaves it zeroed; one workspace per stream).
+ * Replaces the tied fp16 lm_head F.linear + logits[:, -1:].argmax(-1) of
+ * the reference's decode loops (scripts/run_packed.py:164,178,190;
+ * scripts/graph_decode_bench.py:55-112). */
+TP_API int64_t tp_lm_head_workspace_bytes(int64_t B);
+TP_API tp_status tp_lm_head_argmax(const uint16_t* x, const uint16_t* w, int64_t B, int64_t V, int64_t h,
+                                   float* logits, int64_t* idx, float* val, void* workspace,
+                                   int64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Persistent decode engine: a chain of packed linears in ONE launch.
  *

@@ -301,3 +301,13 @@ def random_payload(n: int, d: int, bits: int, n_states: int = 64, seed: int = 0,
         "bias": (rng.standard_normal(n) * 0.1).astype(np.float16) if bias else None,
         "seed": seed,
     }
+
+
+def lm_head_argmax(x: np.ndarray, w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Greedy next token of the reference's decode loops: fp16 lm_head
+    logits then ``logits[:, -1:].argmax(-1)`` (scripts/run_packed.py:164,178,190;
+    scripts/graph_decode_bench.py:55-112), with the logits in float64.
+    Returns (token index per batch row, logits [B, V]); np.argmax keeps the
+    first index among equal logits, as torch.argmax does."""
+    logits = np.asarray(x, dtype=np.float64) @ np.asarray(w, dtype=np.float64).T
+    return np.argmax(logits, axis=-1), logits

@@ -65,6 +65,14 @@ def test_host_only_entry_points(lib):
         _abi.TP_ERR_UNSUPPORTED
     assert L.tp_tcq_gemv(1, 0, 1, 16, 1, 1, None, 1, 0, 1, 16, 256, 256, 3, 12, 1, 1 << 20, None) == \
         _abi.TP_ERR_UNSUPPORTED
+    # greedy LM head: argument checks happen before any device work
+    assert L.tp_lm_head_workspace_bytes(8) >= 8 * 8 + 4
+    assert L.tp_lm_head_argmax(None, 16, 1, 10, 8, None, 16, None, 16, 1024, None) == _abi.TP_ERR_ARG
+    assert L.tp_lm_head_argmax(16, 16, 9, 10, 8, None, 16, None, 16, 1024, None) == _abi.TP_ERR_UNSUPPORTED
+    assert L.tp_lm_head_argmax(16, 16, 1, 10, 12, None, 16, None, 16, 1024, None) == _abi.TP_ERR_ARG
+    assert L.tp_lm_head_argmax(16, 16, 4, 10, 8192, None, 16, None, 16, 1024, None) == _abi.TP_ERR_UNSUPPORTED
+    assert L.tp_lm_head_argmax(16, 17, 1, 10, 8, None, 16, None, 16, 1024, None) == _abi.TP_ERR_ALIGN
+    assert L.tp_lm_head_argmax(16, 16, 1, 10, 8, None, 16, None, 16, 8, None) == _abi.TP_ERR_WORKSPACE
 
 
 def test_module_rejects_cpu_forward():

@@ -168,3 +168,11 @@ def test_bit_sliced_taps_equal_window_decode():
                 sub.append(acc)
             lv = g[f"{key}_member"].astype(np.int64) * 4 + (sub[1] << 1 | sub[0])
             assert np.array_equal(lv.astype(np.uint8), g[f"{key}_levels"])
+
+
+def test_oracle_lm_head_argmax_first_index_on_ties():
+    w = np.zeros((5, 8), dtype=np.float16)
+    w[1] = w[3] = 1.0
+    x = np.ones((2, 8), dtype=np.float16)
+    tok, logits = O.lm_head_argmax(x, w)
+    assert tok.tolist() == [1, 1] and logits.shape == (2, 5) and logits[0, 3] == 8.0

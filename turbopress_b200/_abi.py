@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "tp_tcq_gemv_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P]),
     "tp_gemm_tc_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "tp_tcq_gemm_tc": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _I64, _P]),
+    "tp_lm_head_workspace_bytes": (_I64, [_I64]),
+    "tp_lm_head_argmax": (_I, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P]),
     "tp_engine_image_bytes": (_I64, [_I]),
     "tp_engine_build": (_I, [_P, _I, _I, _I, _I, _P, _P, _I64]),
     "tp_engine_counter_bytes": (_I64, [_I]),
