@@ -174,6 +174,16 @@ __host__ __device__ inline int zperm_pos(int lc) {
   return 2 * (4 * w + (lc >> 3)) + h;
 }
 
+// Shared-memory order of the rotated activations inside a 256-column unit:
+// the 8 halves that one level word w of chunk c pairs with (positions
+// 8w..8w+7 of the chunk's permuted pair order) form 16-byte piece w*8 + c, so
+// the four lanes t that read word w of chunks t (or 4+t) hit 64 contiguous
+// bytes.  tp_rotate mode 3 writes the same order.
+__host__ __device__ inline int64_t sk_zpos(int64_t col) {
+  const int pos = zperm_pos(static_cast<int>(col & 31));
+  return (col & ~int64_t(255)) + (((pos >> 3) * 8 + ((col >> 5) & 7)) << 3) + (pos & 7);
+}
+
 // Bit position, inside member word `word` (0-based after the path word), of
 // member bit `mb` of local column lc (see the GEMV decoder for the use).
 //   bits 2: one word; the 1-bit member of column (8j + r) sits at bit

@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "tp_decode.cuh"
+#include "tp_gemv_sk.cuh"
 #include "tp_rotate.cuh"
 
 namespace cg = cooperative_groups;
@@ -48,11 +49,10 @@ constexpr int kScratchFloats = 8192;    // fp32 FWHT scratch (32 KB)
 constexpr int kMaxSlots = 16;           // weight units in flight per warp
 // dynamic shared memory per CTA (227 KB opt-in minus the static part)
 constexpr size_t kMaxDynSmem = 227u * 1024u - 2048u;
-// The workspace starts with a fixed-size block of split-K counters, so calls
-// of different shapes sharing one workspace never overlap each other's
-// counters with their activation or partial-sum regions.
-constexpr int64_t kMaxRowBlocks = 16384;
-constexpr int64_t kCounterBytes = kMaxRowBlocks * 4;
+// The workspace starts with a fixed-size block of split-K counters (and the
+// status word, tp_gemv_sk.cuh), so calls of different shapes sharing one
+// workspace never overlap each other's counters with their activation or
+// partial-sum regions.
 
 template <int BITS>
 struct Cfg {
@@ -71,6 +71,7 @@ struct GemvParams {
   void* y;
   float* partial;            // [ksplit][B][n_pad] (global split-K only)
   unsigned* counters;        // [row_blocks]      (global split-K only)
+  unsigned* status;          // workspace status word (kStatus* bits)
   int x_dtype, y_dtype;
   int B;
   int64_t n, n_pad, d, d_pad;
@@ -312,7 +313,10 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
         parity ^= 1u;
       }
     }
-    if (!ok) s_fail = 1;  // copies never landed: outputs become NaN below
+    if (!ok) {  // copies never landed: outputs become NaN below
+      s_fail = 1;
+      if (lane == 0) atomicOr(p.status, kStatusTimeout);
+    }
   }
 
   trace(5);
@@ -417,21 +421,6 @@ __global__ void __launch_bounds__(kThreads, 2) tcq_gemv_kernel(GemvParams p) {
 // ---------------------------------------------------------------------------
 // launch configuration
 // ---------------------------------------------------------------------------
-int sm_count() {
-  static std::mutex mu;
-  static int cache[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  std::lock_guard<std::mutex> lk(mu);
-  if (dev >= 64) return 148;
-  if (!cache[dev]) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-    cache[dev] = v;
-  }
-  return cache[dev];
-}
-
 // TP_DEBUG_PLAN=1 prints every launch configuration to stderr.
 bool debug_plans() {
   static const bool on = [] {
@@ -441,7 +430,6 @@ bool debug_plans() {
   return on;
 }
 
-inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 inline uint32_t align128(uint32_t v) { return (v + 127) / 128 * 128; }
 
 struct Plan {
@@ -654,12 +642,35 @@ __global__ void gemv_v2_kernel(const float* __restrict__ z, const uint8_t* __res
 
 }  // namespace
 
+namespace tp {
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+}  // namespace tp
+
 extern "C" int64_t tp_gemv_workspace_bytes(int64_t B, int64_t n, int64_t d, int bits) {
   if (B < 1 || n < 1 || d < 1 || bits < 1 || bits > 4) return -1;
   // Upper bound over every launch plan: counters, pre-rotated activations and
   // partial sums for the largest split along K (32).
   const int64_t Bc = std::min<int64_t>(B, kMaxBatchPerLaunch);
-  return kCounterBytes + align256(Bc * pad_to(d, kUnitCols) * 2) + align256(32 * Bc * pad_to(n, kTileRows) * 4);
+  int64_t extra = align256(Bc * pad_to(d, kUnitCols) * 2) + align256(32 * Bc * pad_to(n, kTileRows) * 4);
+  // the stream-K kernel (batch chunks up to 8) needs its own partial-sum slots
+  // (any Hadamard block: block 1 gives the largest plan)
+  const int64_t sk = sk_workspace_extra(std::min<int64_t>(B, kSkMaxBatch), n, d, bits, 1);
+  if (sk > extra) extra = sk;
+  return kCounterBytes + extra;
 }
 
 extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot_scale, const uint8_t* tcq_stream,
@@ -703,6 +714,27 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
       return fail(TP_ERR_WORKSPACE, "tp_tcq_gemv: plan needs %lld workspace bytes (bound %lld)",
                   (long long)pc.ws_total, (long long)need);
     const void* xc = static_cast<const unsigned char*>(x) + b0 * d * xel;
+    if (Bc <= kSkMaxBatch && sk_workspace_extra(Bc, n, d, bits, block) >= 0) {
+      SkRequest r{};
+      r.x = xc;
+      r.x_dtype = x_dtype;
+      r.rot_scale = rot_scale;
+      r.stream = tcq_stream;
+      r.scales = scales;
+      r.codebook = codebook;
+      r.bias = bias;
+      r.y = static_cast<unsigned char*>(y) + b0 * n * yel;
+      r.y_dtype = y_dtype;
+      r.B = static_cast<int>(Bc);
+      r.n = n;
+      r.d = d;
+      r.block = block;
+      r.bits = bits;
+      r.n_states = n_states;
+      r.workspace = ws;
+      if (tp_status s = sk_gemv(r, st)) return s;
+      continue;
+    }
     GemvParams p{};
     if (!pc.fused_rotation) {
       RotateArgs ra{};
@@ -727,6 +759,7 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
     p.y = static_cast<unsigned char*>(y) + b0 * n * yel;
     p.partial = reinterpret_cast<float*>(ws + kCounterBytes + pc.ws_z);
     p.counters = reinterpret_cast<unsigned*>(ws);
+    p.status = reinterpret_cast<unsigned*>(ws + kStatusOff);
     p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
     p.B = static_cast<int>(Bc);

@@ -8,7 +8,7 @@
 // of this library's device image instead of a caller-provided workspace.
 #include <mutex>
 
-#include "tp_common.cuh"
+#include "tp_gemv_sk.cuh"
 
 using namespace tp;
 
@@ -19,29 +19,27 @@ namespace {
 constexpr int64_t kNoAllocScratchBytes = int64_t(8) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Bytes at the start of the scratch that must be zero before a call: the
-// split-K counter block of tp_tcq_gemv (each call leaves it zero again).
-constexpr size_t kCounterBytes = 16384 * 4;
-
 std::mutex g_mu;
-void* g_scratch_dev[64] = {nullptr};
+void* g_scratch_seen[64] = {nullptr};
 
-// Device address of the scratch array for the current device.  The host-side
-// name g_noalloc_scratch is only a stand-in and must never reach a kernel.
+// Device address of the scratch array for the current device, looked up on
+// every call (cheap on the host) so a reset device or another context never
+// gets a stale pointer.  The host-side name g_noalloc_scratch is only a
+// stand-in and must never reach a kernel.  The first time an address is seen
+// the counter block (tp_gemv_sk.cuh: counters and status word, which every
+// completed call leaves zero) is cleared on `stream`.
 tp_status scratch_for_current_device(void** out, cudaStream_t stream) {
   int dev = 0;
   TP_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  void* p = nullptr;
+  TP_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_dev[dev]) {
-    void* p = nullptr;
-    TP_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
-    // the array starts zeroed; clear the counters anyway so a process that
-    // reloads the module state never starts from stale counts
+  if (g_scratch_seen[dev] != p) {
     TP_CUDA_TRY(cudaMemsetAsync(p, 0, kCounterBytes, stream), "cudaMemsetAsync(noalloc counters)");
-    g_scratch_dev[dev] = p;
+    g_scratch_seen[dev] = p;
   }
-  *out = g_scratch_dev[dev];
+  *out = p;
   return TP_OK;
 }
 

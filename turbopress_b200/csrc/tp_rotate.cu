@@ -16,6 +16,7 @@ namespace tp {
 // mode 1: z = fp16(FWHT(x) * scale), row stride d             (tp_fold_rows)
 // mode 2: z = fp16(FWHT(x * scale)) in the permuted pair layout of the
 //         native GEMV, row stride d_pad, columns [d, d_pad) zeroed
+// mode 3: as mode 2 in the stream-K GEMV's order (sk_zpos)
 __global__ void rotate_kernel(RotateArgs a) {
   extern __shared__ float s[];
   const int64_t row = blockIdx.y;
@@ -40,13 +41,13 @@ __global__ void rotate_kernel(RotateArgs a) {
       v *= h2f_bits(a.scale[c]);
       reinterpret_cast<__half*>(a.z)[row * a.d + c] = __float2half_rn(v);
     } else {
-      const int64_t pos = (c & ~int64_t(31)) + zperm_pos(static_cast<int>(c & 31));
+      const int64_t pos = a.mode == 3 ? sk_zpos(c) : (c & ~int64_t(31)) + zperm_pos(static_cast<int>(c & 31));
       reinterpret_cast<__half*>(a.z)[row * a.d_pad + pos] = __float2half_rn(v);
     }
   }
-  if (a.mode == 2 && blockIdx.x == gridDim.x - 1) {
+  if (a.mode >= 2 && blockIdx.x == gridDim.x - 1) {
     for (int64_t c = a.d + threadIdx.x; c < a.d_pad; c += blockDim.x) {
-      const int64_t pos = (c & ~int64_t(31)) + zperm_pos(static_cast<int>(c & 31));
+      const int64_t pos = a.mode == 3 ? sk_zpos(c) : (c & ~int64_t(31)) + zperm_pos(static_cast<int>(c & 31));
       reinterpret_cast<__half*>(a.z)[row * a.d_pad + pos] = __float2half_rn(0.f);
     }
   }

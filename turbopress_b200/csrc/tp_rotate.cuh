@@ -19,7 +19,7 @@ struct RotateArgs {
   int lg_block;
   int per;  // Hadamard blocks per CTA
   float norm;
-  int mode;  // 0 rotate, 1 fold (post-scale), 2 permuted fp16 for the GEMV
+  int mode;  // 0 rotate, 1 fold (post-scale), 2 permuted fp16 for the GEMV, 3 stream-K GEMV order
 };
 
 // Butterfly stages for index bits [0, lg) over s[0, count) (count a multiple
