@@ -43,6 +43,7 @@ typedef int tp_status;
 #define TP_ERR_ALIGN 3        /* pointer or stride alignment requirement broken */
 #define TP_ERR_CUDA 4         /* a CUDA launch or runtime call failed           */
 #define TP_ERR_WORKSPACE 6    /* workspace missing or smaller than required     */
+#define TP_ERR_DEVICE 7       /* a kernel reported a device-side failure        */
 
 /* Activation / output element types. */
 #define TP_F16 0
@@ -302,6 +303,72 @@ TP_API tp_status tp_ipc_close(void* ptr);
  * host image it was copied from). */
 TP_API tp_status tp_engine_run(const void* image_dev, const void* image_host, unsigned* counters,
                                void* stream);
+
+/* ------------------------------------------------------------------------
+ * Decoder step: one cooperative launch runs a whole batch-B decode step of
+ * a Qwen3 / Llama-style decoder whose seven linears per layer are packed TCQ
+ * (bits 2..4, 64 states): per layer RMSNorm -> q/k/v -> (Qwen3 q/k head
+ * norms) -> RoPE -> KV-cache append -> GQA attention over positions
+ * [0, pos] -> o_proj + residual -> RMSNorm -> gate/up -> SiLU(gate)*up ->
+ * down_proj + residual, and the final RMSNorm.  fp16 activations, rounded
+ * where the reference model's fp16 forward rounds them (the LM head follows
+ * as tp_lm_head_argmax on final_out).  Replaces the decoder forward that the
+ * reference runs with PackedTCQLinear layers inside a Hugging Face model
+ * (turbopress/runtime.py:455-541 load_packed_model, stepped by
+ * scripts/run_packed.py:160-190 and scripts/graph_decode_bench.py:70-118).
+ * ---------------------------------------------------------------------- */
+typedef struct tp_step_linear {
+  const uint8_t* tcq_stream;  /* native stream (tp_relayout_v2 / _v1), 16-byte aligned */
+  const uint16_t* scales;     /* fp16 [n]                                             */
+  const uint16_t* codebook;   /* fp16 [2^(bits+1)]                                    */
+  const uint16_t* rot_scale;  /* fp16 [d], 16-byte aligned                            */
+  const uint16_t* bias;       /* fp16 [n] or NULL                                     */
+  int64_t n, d, block;        /* block: Hadamard block, 256..8192                     */
+  int32_t bits, n_states;
+} tp_step_linear;
+
+typedef struct tp_step_layer {
+  tp_step_linear q, k, v, o, gate, up, down;
+  const uint16_t* ln1;      /* input_layernorm weight, fp16 [hidden]                 */
+  const uint16_t* ln2;      /* post_attention_layernorm weight                       */
+  const uint16_t* q_norm;   /* fp16 [head_dim] (Qwen3) or NULL                       */
+  const uint16_t* k_norm;
+  uint16_t* k_cache;        /* fp16 [B][kv_heads][max_tokens][head_dim], post-RoPE   */
+  uint16_t* v_cache;
+} tp_step_layer;
+
+typedef struct tp_step_model {
+  int32_t B, layers, hidden, inter, q_heads, kv_heads, head_dim, max_tokens;
+  float rms_eps;
+  const float* inv_freq;        /* fp32 [head_dim/2] RoPE inverse frequencies        */
+  const uint16_t* final_norm;   /* fp16 [hidden]                                     */
+  uint16_t* hidden_state;       /* fp16 [B][hidden]: input embeddings in, residual   */
+  uint16_t* final_out;          /* fp16 [B][hidden]: final RMSNorm output            */
+  void* act;                    /* tp_step_act_bytes() bytes of activation scratch   */
+} tp_step_model;
+
+/* Bytes of the step program image for `layers` layers / of the activation
+ * scratch the model needs. */
+TP_API int64_t tp_step_image_bytes(int layers);
+TP_API int64_t tp_step_act_bytes(const tp_step_model* m);
+
+/* Build the program image in HOST memory for the current device (no device
+ * work); *workspace_bytes receives the workspace size tp_step_run needs (zero
+ * it once; each run leaves its counters at zero).  Copy the image to a
+ * 16-byte aligned device buffer of the same size. */
+TP_API tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* layers, void* image_host,
+                               int64_t image_bytes, int64_t* workspace_bytes);
+
+/* One decode step at position *pos_dev (device int: the number of tokens
+ * already in the caches; the step writes k/v at that position).  Enqueued on
+ * `stream` (graph-capturable: a 4-byte memset and one cooperative launch). */
+TP_API tp_status tp_step_run(const void* image_dev, const void* image_host, const int* pos_dev,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Reads (synchronizing `stream`) and clears the device status word of a
+ * step workspace: TP_OK, or TP_ERR_DEVICE when a grid barrier timed out or
+ * the shared-memory layout check failed. */
+TP_API tp_status tp_step_status(const void* workspace, void* stream);
 
 /* Reference-order GEMV straight from the format-v2 streams, any bits in 1..7:
  * y[B, n] = z[B, d] @ decode_rows^T (+ bias), z fp32 rotated activations.

@@ -18,6 +18,7 @@ _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
 TP_OK, TP_ERR_ARG, TP_ERR_UNSUPPORTED, TP_ERR_ALIGN, TP_ERR_CUDA, TP_ERR_WORKSPACE = 0, 1, 2, 3, 4, 6
+TP_ERR_DEVICE = 7
 TP_F16, TP_F32, TP_BF16 = 0, 1, 2
 
 _P = ctypes.c_void_p
@@ -58,6 +59,11 @@ SIGNATURES: dict[str, tuple] = {
     "tp_ipc_open": (_I, [_P, _P]),
     "tp_ipc_close": (_I, [_P]),
     "tp_gemv_v2": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _I, _P]),
+    "tp_step_image_bytes": (_I64, [_I]),
+    "tp_step_act_bytes": (_I64, [_P]),
+    "tp_step_build": (_I, [_P, _P, _P, _I64, _P]),
+    "tp_step_run": (_I, [_P, _P, _P, _P, _I64, _P]),
+    "tp_step_status": (_I, [_P, _P]),
 }
 
 
