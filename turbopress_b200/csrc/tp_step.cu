@@ -43,16 +43,18 @@ constexpr int kStepThreads = kStepWarps * 32;
 constexpr int kMaxStageOps = 3;
 constexpr int kStepMaxBatch = 8;
 constexpr int kMaxGroup = 8;        // query heads per kv head
-constexpr unsigned kBarrierPolls = 1u << 24;  // x ~64 ns sleep: about a second
+constexpr int kMaxSplits = 32;      // attention splits per (batch row, kv head)
+constexpr unsigned long long kBarrierNs = 2000000000ull;  // a grid barrier gives up after 2 s
 
 enum StageType : int { kLinear = 0, kAttention = 1, kFinalNorm = 2 };
 enum InKind : int { kInPlain = 0, kInRmsNorm = 1, kInSiluMul = 2 };
 enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1 };
 
 // workspace words
-constexpr int64_t kWsBarrier = 0;     // grid barrier counter (reset before each run)
-constexpr int64_t kWsStatus = 64;     // status bits (kStepStatus*)
-constexpr int64_t kWsCounters = 256;  // per-row-tile / per-attention-group counters
+constexpr int64_t kWsStatus = 64;      // status bits (kStepStatus*)
+constexpr int64_t kWsFlags = 1024;     // grid barrier counter (zeroed before each run)
+constexpr int kMaxGrid = 512;
+constexpr int64_t kWsCounters = kWsFlags + 4 * kMaxGrid;  // per-row-tile / per-attention-group counters
 constexpr unsigned kStepStatusLayout = 1u, kStepStatusBarrier = 2u;
 
 struct alignas(16) StepOp {
@@ -72,8 +74,8 @@ struct alignas(16) LinearStage {
   int nops, in_kind, epi, bits;
   int d, d_pad, units_k, lg_block;
   float norm, eps;
-  int kparts, us, cps, maxc, rt_total, rpp;
-  uint32_t z_off, xin_off, scr_off, pad;  // shared-memory offsets from the dynamic base
+  int kparts, us, cps, maxc, rt_total, rpp, rs_smem, pad2[3];
+  uint32_t z_off, xin_off, scr_off, rs_off;  // shared-memory offsets from the dynamic base
   SliceSplit split[2];
   StepOp ops[kMaxStageOps];
 };
@@ -125,6 +127,21 @@ constexpr int kMiscFlags = 1792;   // barrier / last-CTA flags
 constexpr int kMiscBytes = 2048;
 static_assert(sizeof(StepStage) <= 1024, "stage record");
 
+#ifdef TP_STEP_TRACE
+// Development-only stage timeline (built only with -DTP_STEP_TRACE, never in
+// the shipped library): %globaltimer per stage, CTA and phase.
+__device__ unsigned long long g_step_trace[256][160][4];
+__device__ __forceinline__ void step_trace(int s, int k) {
+  if (threadIdx.x == 0 && blockIdx.x < 160 && s < 256) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_step_trace[s][blockIdx.x][k] = t;
+  }
+}
+#else
+__device__ __forceinline__ void step_trace(int, int) {}
+#endif
+
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 __device__ __forceinline__ float r16(float v) { return __half2float(__float2half_rn(v)); }
@@ -135,21 +152,29 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
-// Grid barrier on a cumulative counter: every CTA adds one, then waits for
-// `target`.  Bounded: gives up (status + abort) after kBarrierPolls polls.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Grid barrier on a cumulative arrival counter: one thread per CTA adds one
+// (after a release fence) and spins on acquire loads until `target`; bounded
+// by kBarrierNs of global time, after which it sets the status and every
+// CTA abandons the step.
 __device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, int* s_ok) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(bar, 1u);
     int ok = 0;
-    for (unsigned i = 0; i < kBarrierPolls; ++i) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 0;; ++i) {
       if (ld_acquire(bar) >= target) {
         ok = 1;
         break;
       }
-      if (ld_acquire(status) & kStepStatusBarrier) break;
-      __nanosleep(64);
+      if ((i & 255u) == 255u && (global_ns() - t0 > kBarrierNs || (ld_acquire(status) & kStepStatusBarrier))) break;
     }
     if (!ok) atomicOr(status, kStepStatusBarrier);
     *s_ok = ok;
@@ -161,49 +186,129 @@ __device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, i
 // ---------------------------------------------------------------------------
 // linear stage
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ float sumsq8(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+    s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
+  }
+  return s;
+}
+
 // Input transform of rows [b0, b0+rows) over slice columns [c0, c0+cols):
-// xin (fp16 bits, [rows][cols]) = the stage's input as the reference rounds it.
-__device__ void stage_input(const LinearStage& L, int B, int b0, int rows, int c0, int cols, uint16_t* xin,
-                            float* red) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (L.in_kind == kInRmsNorm) {
-    // mean of squares over the whole row (every CTA; the rows are short)
-    for (int b = 0; b < rows; ++b) {
-      const uint16_t* x = L.in0 + (int64_t)(b0 + b) * L.d;
-      float s = 0.f;
-      for (int c = tid * 2; c < L.d; c += kStepThreads * 2) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(x + c));
-        s += f.x * f.x + f.y * f.y;
-      }
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) red[b * kStepWarps + warp] = s;
+// xin (fp16 bits, [rows][cols]) = the stage's input as the reference rounds
+// it.  Every thread issues all of its 16-byte loads of a round before using
+// them (one memory round trip per round of 512 chunks of 8 columns).
+__device__ __forceinline__ uint4 transform8(int kind, uint4 xv, uint4 uv, uint4 gv, float r) {
+  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+  uint32_t ow[4];
+  if (kind == kInRmsNorm) {
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+      const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&gw[e]));
+      const __half2 hv = __floats2half2_rn(gf.x * r16(xf.x * r), gf.y * r16(xf.y * r));
+      ow[e] = *reinterpret_cast<const uint32_t*>(&hv);
     }
+  } else if (kind == kInSiluMul) {
+    const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+      const float2 uf = __half22float2(*reinterpret_cast<const __half2*>(&uw[e]));
+      const float a0 = r16(gf.x / (1.f + __expf(-gf.x))), a1 = r16(gf.y / (1.f + __expf(-gf.y)));
+      const __half2 hv = __floats2half2_rn(a0 * uf.x, a1 * uf.y);
+      ow[e] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ow[e] = xw[e];
+  }
+  return make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+// Input transform of rows [b0, b0+rows) over slice columns [c0, c0+cols):
+// xin (fp16 bits, [rows][cols]) = the stage's input as the reference rounds
+// it.  Warps split over the rows (fixed order: deterministic sums); every
+// lane issues all its 16-byte loads of a round before using them, and when a
+// row fits one round the norm's sum of squares comes from the same loads.
+__device__ __forceinline__ void stage_input(const LinearStage& L, int b0, int rows, int c0, int cols,
+                                            uint16_t* xin, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* rinv = red + kStepMaxBatch * kStepWarps;
+  const int wpr = kStepWarps / rows, row = warp / wpr, sub = warp - row * wpr;
+  const bool act = row < rows;
+  const int64_t xrow = (int64_t)(b0 + (act ? row : 0)) * L.d;
+  constexpr int U = 4;  // 16-byte loads per lane in flight
+  const int stride = wpr * 32;
+  const int cpr = cols >> 3;
+  const bool norm = L.in_kind == kInRmsNorm;
+  // one round covers the whole row: load once, norm from the same registers
+  const bool single = cols == L.d && cpr <= stride * U;
+  uint4 xv[U], uv[U], gv[U];
+  auto load_round = [&](int cb) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int ci = cb + u * stride, c = c0 + ci * 8;
+      if (act && ci < cpr && c < L.d) {
+        xv[u] = *reinterpret_cast<const uint4*>(L.in0 + xrow + c);
+        if (L.in_kind == kInSiluMul) uv[u] = *reinterpret_cast<const uint4*>(L.in1 + xrow + c);
+        if (norm) gv[u] = *reinterpret_cast<const uint4*>(L.gamma + c);
+      }
+    }
+  };
+  if (single) load_round(sub * 32 + lane);
+  if (norm) {
+    float ssum = 0.f;
+    if (single) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int ci = sub * 32 + lane + u * stride;
+        if (act && ci < cpr) ssum += sumsq8(xv[u]);
+      }
+    } else {
+      const int dpr = L.d >> 3;
+      for (int cb = sub * 32 + lane; act && cb < dpr; cb += stride * U) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (cb + u * stride < dpr) v[u] = *reinterpret_cast<const uint4*>(L.in0 + xrow + (cb + u * stride) * 8);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (cb + u * stride < dpr) ssum += sumsq8(v[u]);
+      }
+    }
+    for (int o = 16; o; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    if (lane == 0) red[warp] = ssum;
     __syncthreads();
     if (tid < rows) {
-      float s = 0.f;
-      for (int w = 0; w < kStepWarps; ++w) s += red[tid * kStepWarps + w];
-      red[kStepMaxBatch * kStepWarps + tid] = rsqrtf(s / (float)L.d + L.eps);
+      float sv = 0.f;
+      for (int w = 0; w < wpr; ++w) sv += red[tid * wpr + w];
+      rinv[tid] = rsqrtf(sv / (float)L.d + L.eps);
     }
     __syncthreads();
   }
-  for (int i = tid; i < rows * cols; i += kStepThreads) {
-    const int b = i / cols, c = c0 + (i - b * cols);
-    uint16_t o = 0;
-    if (c < L.d) {
-      const int64_t xi = (int64_t)(b0 + b) * L.d + c;
-      if (L.in_kind == kInRmsNorm) {
-        const float xn = r16(h2f(L.in0[xi]) * red[kStepMaxBatch * kStepWarps + b]);
-        o = f2h(h2f(L.gamma[c]) * xn);
-      } else if (L.in_kind == kInSiluMul) {
-        const float gte = h2f(L.in0[xi]);
-        const float act = r16(gte / (1.f + __expf(-gte)));
-        o = f2h(act * h2f(L.in1[xi]));
-      } else {
-        o = L.in0[xi];
-      }
+  const float r = norm && act ? rinv[row] : 1.f;
+  for (int cb = sub * 32 + lane; act && cb < cpr; cb += stride * U) {
+    if (!single) load_round(cb);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int ci = cb + u * stride, c = c0 + ci * 8;
+      if (ci >= cpr) break;
+      const uint4 o = c < L.d ? transform8(L.in_kind, xv[u], uv[u], gv[u], r) : make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(xin + row * cols + ci * 8) = o;
     }
-    xin[i] = o;
   }
+  cp_async_wait_all();  // the rotation scales of the stage (issued before its barrier)
   __syncthreads();
 }
 
@@ -225,7 +330,7 @@ __device__ __forceinline__ void step_column_pass(const float* scr, __half* z, in
 }
 
 // z rows [b0, b0+rows) of one op: FWHT(xin * rot_scale) per Hadamard block.
-__device__ void stage_rotate(const LinearStage& L, const uint16_t* rs, const uint16_t* xin, int rows, int c0,
+__device__ __forceinline__ void stage_rotate(const LinearStage& L, const uint16_t* rs, const uint16_t* xin, int rows, int c0,
                              int cols, float* scr, __half* z, int zst) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lg = L.lg_block, tpr = cols >> 8;
@@ -234,8 +339,9 @@ __device__ void stage_rotate(const LinearStage& L, const uint16_t* rs, const uin
     float v[8];
     const uint4 xv = *reinterpret_cast<const uint4*>(xin + rr * cols + cl);
     const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    // slice-local scales (shared memory: zero past d; global: guarded)
     uint4 rv = make_uint4(0u, 0u, 0u, 0u);
-    if (c0 + cl < L.d) rv = *reinterpret_cast<const uint4*>(rs + c0 + cl);
+    if (L.rs_smem || c0 + cl < L.d) rv = *reinterpret_cast<const uint4*>(rs + cl);
     const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -274,9 +380,102 @@ __device__ void stage_rotate(const LinearStage& L, const uint16_t* rs, const uin
   }
 }
 
+// Hadamard blocks of 256 or 512 columns, every op at once: one warp per
+// (op, row, block) holds the block in registers (E = 8 or 16 columns per
+// lane: the low index bits in place, the five lane bits by shuffles) and
+// writes the fp16 activations; no shared-memory staging, one barrier.
+template <int E>
+__device__ __forceinline__ void rotate_small_blocks(const LinearStage& L, const uint16_t* rs_all, int rs_stride,
+                                                    const uint16_t* xin, int rows, int b0, int B, int c0, int cols,
+                                                    __half* z, int zst) {
+  constexpr int LGE = E == 16 ? 4 : 3;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int blk = 32 * E, nblk = cols / blk, per_op = rows * nblk;
+  for (int task = warp; task < L.nops * per_op; task += kStepWarps) {
+    const int k = task / per_op, rem = task - k * per_op, rr = rem / nblk, bi = rem - rr * nblk;
+    const int cl = bi * blk + lane * E;
+    const uint16_t* rs = rs_all + (int64_t)k * rs_stride;
+    float v[E];
+#pragma unroll
+    for (int q = 0; q < E / 8; ++q) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(xin + rr * cols + cl + 8 * q);
+      uint4 rv = make_uint4(0u, 0u, 0u, 0u);
+      if (L.rs_smem || c0 + cl + 8 * q < L.d) rv = *reinterpret_cast<const uint4*>(rs + cl + 8 * q);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+        const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[e]));
+        v[8 * q + 2 * e] = xf.x * rf.x;
+        v[8 * q + 2 * e + 1] = xf.y * rf.y;
+      }
+    }
+    fwht_regs<LGE>(v);
+#pragma unroll
+    for (int sbit = 0; sbit < 5; ++sbit) {
+      const float sg = (lane >> sbit) & 1 ? -1.f : 1.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = fmaf(sg, v[e], __shfl_xor_sync(0xffffffffu, v[e], 1 << sbit));
+    }
+    __half* zr = z + (k * (B + 1) + b0 + rr) * zst;
+#pragma unroll
+    for (int e = 0; e < E; ++e) zr[sk_zpos(cl + e)] = __float2half_rn(v[e] * L.norm);
+  }
+  __syncthreads();
+}
+
+// Rotation scales of a linear stage into shared memory (cp.async, waited for
+// in stage_input): issued before the barrier that precedes the stage, they
+// depend on nothing the barrier orders.
+__device__ void stage_rs_prefetch(const LinearStage& L, unsigned char* smem) {
+  const int slice = blockIdx.x / L.cps;
+  if (slice >= L.kparts || !L.rs_smem) return;
+  const int Us = L.split[slice == L.kparts - 1 ? 1 : 0].us;
+  const int cols = Us * kUnitCols, c0 = slice * L.us * kUnitCols;
+  uint16_t* rs_s = reinterpret_cast<uint16_t*>(smem + L.rs_off);
+  for (int i = threadIdx.x; i < L.nops * (cols / 8); i += kStepThreads) {
+    const int k = i / (cols / 8), ci = i - k * (cols / 8);
+    const bool valid = c0 + ci * 8 < L.d;
+    cp_async16(rs_s + k * cols + ci * 8, L.ops[k].rot_scale + (valid ? c0 + ci * 8 : 0), valid);
+  }
+}
+
+// Stage prologue: rotation scales to shared memory (async), the input
+// transform, every op's rotated activations, and the zero rows (CTAs of a
+// K-slice: the slice's columns).
+__device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
+  const int tid = threadIdx.x;
+  const int slice = blockIdx.x / L.cps;
+  if (slice >= L.kparts) return;
+  const int Us = L.split[slice == L.kparts - 1 ? 1 : 0].us;
+  const int cols = Us * kUnitCols, c0 = slice * L.us * kUnitCols;
+  const int zst = L.us * kUnitCols + kZPad;
+  __half* z = reinterpret_cast<__half*>(smem + L.z_off);
+  uint16_t* xin = reinterpret_cast<uint16_t*>(smem + L.xin_off);
+  float* scr = reinterpret_cast<float*>(smem + L.scr_off);
+  uint16_t* rs_s = reinterpret_cast<uint16_t*>(smem + L.rs_off);
+  for (int b0 = 0; b0 < B; b0 += L.rpp) {
+    const int rows = min(L.rpp, B - b0);
+    stage_input(L, b0, rows, c0, cols, xin, red);
+    if (L.lg_block <= 9 && L.rs_smem) {
+      if (L.lg_block == 9) rotate_small_blocks<16>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
+      else rotate_small_blocks<8>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
+    } else {
+      for (int k = 0; k < L.nops; ++k)
+        stage_rotate(L, L.rs_smem ? rs_s + k * cols : L.ops[k].rot_scale + c0, xin, rows, c0, cols, scr,
+                     z + (k * (B + 1) + b0) * zst, zst);
+    }
+  }
+  for (int i = tid; i < L.nops * (cols / 8); i += kStepThreads) {
+    const int k = i / (cols / 8), r = i - k * (cols / 8);
+    reinterpret_cast<uint4*>(z + (k * (B + 1) + B) * zst)[r] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncthreads();
+}
+
 template <int BITS>
-__device__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
-                             unsigned char* ws, const StepHeader& H) {
+__device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
+                             unsigned char* ws, const StepHeader& H, int sidx) {
   constexpr int S = 64;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -300,7 +499,12 @@ __device__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, c
     return L.ops[k].stream + ((int64_t)(rt - L.ops[k].rt_off) * L.units_k + us0 + ul) * UB;
   };
 
-  // ---- first unit of the run and its trellis halo ----
+  // the rotated activations were built by stage_prologue (called before)
+  const int zst = L.us * kUnitCols + kZPad;
+  __half* z = reinterpret_cast<__half*>(smem + L.z_off);
+
+  // ---- first unit of the run and its trellis halo (in L2: prefetched
+  // before the barrier) ----
   int rt = sp.row_tile(j0), ul = j0 - rt * Us;
   int opk = op_of(rt);
   uint4 wa[BITS];
@@ -315,25 +519,7 @@ __device__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, c
       hq = pv.w;
     }
   }
-
-  // ---- input transform and rotation into z (per op) ----
-  const int cols = Us * kUnitCols, c0 = us0 * kUnitCols;
-  const int zst = L.us * kUnitCols + kZPad;
-  __half* z = reinterpret_cast<__half*>(smem + L.z_off);
-  uint16_t* xin = reinterpret_cast<uint16_t*>(smem + L.xin_off);
-  float* scr = reinterpret_cast<float*>(smem + L.scr_off);
-  float* red = reinterpret_cast<float*>(smem + H.misc_off + kMiscRed);
-  for (int b0 = 0; b0 < B; b0 += L.rpp) {
-    const int rows = min(L.rpp, B - b0);
-    stage_input(L, B, b0, rows, c0, cols, xin, red);
-    for (int k = 0; k < L.nops; ++k)
-      stage_rotate(L, L.ops[k].rot_scale, xin, rows, c0, cols, scr, z + (k * (B + 1) + b0) * zst, zst);
-  }
-  for (int i = tid; i < L.nops * (cols / 8); i += kStepThreads) {
-    const int k = i / (cols / 8), r = i - k * (cols / 8);
-    reinterpret_cast<uint4*>(z + (k * (B + 1) + B) * zst)[r] = make_uint4(0u, 0u, 0u, 0u);
-  }
-  __syncthreads();
+  step_trace(sidx, 1);
 
   // ---- decode + MMA over the run ----
   float acc[2][4];
@@ -489,29 +675,28 @@ __device__ void prefetch_stage(const LinearStage& L) {
 // RMS norm of one head vector held E values per lane (the whole warp), fp16
 // rounding as the reference: fp16(gamma * fp16(x * rsqrt(mean(x^2) + eps))).
 template <int E>
-__device__ __forceinline__ void head_norm(float* x, const uint16_t* gamma, int hd, float eps, int lane) {
+__device__ __forceinline__ void head_norm(float* x, const float* gam, int hd, float eps) {
   float s = 0.f;
 #pragma unroll
   for (int e = 0; e < E; ++e) s += x[e] * x[e];
   for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float r = rsqrtf(s / (float)hd + eps);
 #pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = r16(h2f(gamma[lane * E + e]) * r16(x[e] * r));
+  for (int e = 0; e < E; ++e) x[e] = r16(gam[e] * r16(x[e] * r));
 }
 
-// RoPE (rotate-half form) at position pos on a head vector (E values per
-// lane, lanes 0-15 hold the first half): fp16(fp16(x*cos) + fp16(rot*sin)),
-// cos / sin rounded to fp16.
+// RoPE (rotate-half form) on a head vector (E values per lane, lanes 0-15
+// hold the first half): fp16(fp16(x*cos) + fp16(rot*sin)), cos / sin of
+// pos * inv_freq rounded to fp16.
 template <int E>
-__device__ __forceinline__ void rope(float* x, const float* inv_freq, int pos, int lane) {
+__device__ __forceinline__ void rope(float* x, const float* freq, int pos, int lane) {
   float partner[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
   const bool hi = lane >= 16;
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const int i = (lane & 15) * E + e;  // frequency index
-    const float f = (float)pos * inv_freq[i];
+    const float f = (float)pos * freq[e];
     const float c = r16(cosf(f)), s = r16(sinf(f));
     const float rot = hi ? partner[e] : -partner[e];
     x[e] = r16(r16(x[e] * c) + r16(rot * s));
@@ -519,7 +704,20 @@ __device__ __forceinline__ void rope(float* x, const float* inv_freq, int pos, i
 }
 
 template <int E>
-__device__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, unsigned char* buf, float* part,
+__device__ __forceinline__ void load_h(float* v, const uint16_t* p) {
+  if constexpr (E == 4) {
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+    v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+  } else {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = a.x, v[1] = a.y;
+  }
+}
+
+template <int E, int G>
+__device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, unsigned char* buf, float* part,
                           unsigned* counters, int cgroup, unsigned* s_last) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hd = A.hd, gs = A.q_heads / A.kv_heads;
@@ -529,38 +727,48 @@ __device__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, u
   float* wst = vnew + hd;                                    // [16 warps][gs][hd + 2]
   const int T = pos + 1, Ls = (T + A.nsplit - 1) / A.nsplit;
   const int t0 = sp * Ls, t1 = min(T, t0 + Ls);
+  const int64_t kv0 = ((int64_t)b * A.kv_heads + kvh) * A.max_t;
+  // this warp's first cached token, loaded before anything waits
+  float kx[E], vx[E];
+  int tok = t0 + warp;
+  if (tok < t1 && tok != pos) {
+    load_h<E>(kx, A.k_cache + (kv0 + tok) * hd + lane * E);
+    load_h<E>(vx, A.v_cache + (kv0 + tok) * hd + lane * E);
+  }
   // q heads of the group (one warp per head) and the new token's k / v
-  if (warp < gs) {
-    float x[E];
-    const uint16_t* q = A.q + (int64_t)b * A.q_heads * hd + (kvh * gs + warp) * hd;
+  const bool newtok = t1 == T && t0 < t1;
+  if (warp < gs || (warp == kStepWarps - 1 && newtok)) {
+    const bool isq = warp < gs;
+    const uint16_t* src = isq ? A.q + (int64_t)b * A.q_heads * hd + (kvh * gs + warp) * hd
+                              : A.k + (int64_t)b * A.kv_heads * hd + kvh * hd;
+    const uint16_t* gam = isq ? A.q_norm : A.k_norm;
+    float x[E], gm[E], fr[E], vv[E];
+    load_h<E>(x, src + lane * E);
+    if (gam) load_h<E>(gm, gam + lane * E);
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = h2f(q[lane * E + e]);
-    if (A.q_norm) head_norm<E>(x, A.q_norm, hd, A.eps, lane);
-    rope<E>(x, A.inv_freq, pos, lane);
+    for (int e = 0; e < E; ++e) fr[e] = A.inv_freq[(lane & 15) * E + e];
+    if (!isq) load_h<E>(vv, A.v + (int64_t)b * A.kv_heads * hd + kvh * hd + lane * E);
+    if (gam) head_norm<E>(x, gm, hd, A.eps);
+    rope<E>(x, fr, pos, lane);
+    if (isq) {
 #pragma unroll
-    for (int e = 0; e < E; ++e) sq[warp * hd + lane * E + e] = x[e];
-  } else if (warp == kStepWarps - 1 && t1 == T && t0 < t1) {
-    float x[E];
-    const uint16_t* k = A.k + (int64_t)b * A.kv_heads * hd + kvh * hd;
-    const uint16_t* v = A.v + (int64_t)b * A.kv_heads * hd + kvh * hd;
+      for (int e = 0; e < E; ++e) sq[warp * hd + lane * E + e] = x[e];
+    } else {
+      const int64_t ci = (kv0 + pos) * hd;
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = h2f(k[lane * E + e]);
-    if (A.k_norm) head_norm<E>(x, A.k_norm, hd, A.eps, lane);
-    rope<E>(x, A.inv_freq, pos, lane);
-    const int64_t ci = (((int64_t)b * A.kv_heads + kvh) * A.max_t + pos) * hd;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      knew[lane * E + e] = x[e];
-      vnew[lane * E + e] = h2f(v[lane * E + e]);
-      A.k_cache[ci + lane * E + e] = f2h(x[e]);
-      A.v_cache[ci + lane * E + e] = v[lane * E + e];
+      for (int e = 0; e < E; ++e) {
+        knew[lane * E + e] = x[e];
+        vnew[lane * E + e] = vv[e];
+        A.k_cache[ci + lane * E + e] = f2h(x[e]);
+        A.v_cache[ci + lane * E + e] = f2h(vv[e]);
+      }
     }
   }
   __syncthreads();
   // per-warp online softmax over its tokens
-  float qv[kMaxGroup][E], m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][E];
+  float qv[G][E], m[G], l[G], acc[G][E];
 #pragma unroll
-  for (int j = 0; j < kMaxGroup; ++j) {
+  for (int j = 0; j < G; ++j) {
     m[j] = -INFINITY;
     l[j] = 0.f;
 #pragma unroll
@@ -569,49 +777,41 @@ __device__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, u
       acc[j][e] = 0.f;
     }
   }
-  const int64_t kv0 = ((int64_t)b * A.kv_heads + kvh) * A.max_t;
-  for (int tok = t0 + warp; tok < t1; tok += kStepWarps) {
-    float kx[E], vx[E];
+  for (; tok < t1; tok += kStepWarps) {
     if (tok == pos) {
 #pragma unroll
       for (int e = 0; e < E; ++e) kx[e] = knew[lane * E + e], vx[e] = vnew[lane * E + e];
-    } else {
-      const uint16_t* kr = A.k_cache + (kv0 + tok) * hd + lane * E;
-      const uint16_t* vr = A.v_cache + (kv0 + tok) * hd + lane * E;
-      if constexpr (E == 4) {
-        const uint2 kk = *reinterpret_cast<const uint2*>(kr), vv = *reinterpret_cast<const uint2*>(vr);
-        const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
-        const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
-        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv.x));
-        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv.y));
-        kx[0] = k0.x, kx[1] = k0.y, kx[2] = k1.x, kx[3] = k1.y;
-        vx[0] = v0.x, vx[1] = v0.y, vx[2] = v1.x, vx[3] = v1.y;
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) kx[e] = h2f(kr[e]), vx[e] = h2f(vr[e]);
-      }
+    }
+    // next token's k / v in flight while this one is used
+    float kn[E], vn[E];
+    const int nt = tok + kStepWarps;
+    if (nt < t1 && nt != pos) {
+      load_h<E>(kn, A.k_cache + (kv0 + nt) * hd + lane * E);
+      load_h<E>(vn, A.v_cache + (kv0 + nt) * hd + lane * E);
     }
 #pragma unroll
-    for (int j = 0; j < kMaxGroup; ++j) {
+    for (int j = 0; j < G; ++j) {
       if (j >= gs) break;
-      float s = 0.f;
+      float sc = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; ++e) s = fmaf(qv[j][e], kx[e], s);
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      for (int e = 0; e < E; ++e) sc = fmaf(qv[j][e], kx[e], sc);
+      for (int o = 16; o; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
       // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
-      s = r16(r16(s) * A.scaling);
-      const float mn = fmaxf(m[j], s);
-      const float corr = __expf(m[j] - mn), p = __expf(s - mn);
+      sc = r16(r16(sc) * A.scaling);
+      const float mn = fmaxf(m[j], sc);
+      const float corr = __expf(m[j] - mn), p = __expf(sc - mn);
       l[j] = l[j] * corr + p;
 #pragma unroll
       for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[e]);
       m[j] = mn;
     }
+#pragma unroll
+    for (int e = 0; e < E; ++e) kx[e] = kn[e], vx[e] = vn[e];
   }
   // combine the warps
   const int ws_ = hd + 2;
 #pragma unroll
-  for (int j = 0; j < kMaxGroup; ++j) {
+  for (int j = 0; j < G; ++j) {
     if (j >= gs) break;
     float* dst = wst + (warp * gs + j) * ws_;
 #pragma unroll
@@ -640,24 +840,35 @@ __device__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, u
   // the last CTA of the (b, kvh) group combines the splits
   __threadfence();
   __syncthreads();
-  if (tid == 0) {
-    *s_last = atomicAdd(&counters[cgroup], 1u) == (unsigned)(A.nsplit - 1) ? 1u : 0u;
-  }
+  if (tid == 0) *s_last = atomicAdd(&counters[cgroup], 1u) == (unsigned)(A.nsplit - 1) ? 1u : 0u;
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
   const float* gp = part + (int64_t)cgroup * A.nsplit * gs * ws_;
+  // split maxima and sums into shared memory first (one pass of loads)
+  float* ml = wst;  // [nsplit][gs][2]
+  for (int i = tid; i < A.nsplit * gs; i += kStepThreads) {
+    ml[2 * i] = __ldcg(gp + i * ws_);
+    ml[2 * i + 1] = __ldcg(gp + i * ws_ + 1);
+  }
+  __syncthreads();
   for (int i = tid; i < gs * hd; i += kStepThreads) {
     const int j = i / hd, dd = i - j * hd;
     float M = -INFINITY;
-    for (int s2 = 0; s2 < A.nsplit; ++s2) M = fmaxf(M, __ldcg(gp + (s2 * gs + j) * ws_));
+    for (int s2 = 0; s2 < A.nsplit; ++s2) M = fmaxf(M, ml[2 * (s2 * gs + j)]);
+    // every split's partial in flight at once, then the weighted sum
+    float av[kMaxSplits];
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxSplits; ++s2)
+      if (s2 < A.nsplit) av[s2] = __ldcg(gp + (s2 * gs + j) * ws_ + 2 + dd);
     float Lsum = 0.f, Ad = 0.f;
-    for (int s2 = 0; s2 < A.nsplit; ++s2) {
-      const float* src = gp + (s2 * gs + j) * ws_;
-      const float ms = __ldcg(src);
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxSplits; ++s2) {
+      if (s2 >= A.nsplit) break;
+      const float ms = ml[2 * (s2 * gs + j)];
       const float f = ms == -INFINITY ? 0.f : __expf(ms - M);
-      Lsum += __ldcg(src + 1) * f;
-      Ad += __ldcg(src + 2 + dd) * f;
+      Lsum += ml[2 * (s2 * gs + j) + 1] * f;
+      Ad += av[s2] * f;
     }
     A.out[(int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd] = f2h(Ad / Lsum);
   }
@@ -674,8 +885,14 @@ __device__ void attn_stage(const AttnStage& A, int B, int pos, unsigned char* sm
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int grp = it / A.nsplit, sp = it - grp * A.nsplit;
     const int b = grp / A.kv_heads, kvh = grp - b * A.kv_heads;
-    if (A.hd == 128) attn_item<4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
-    else attn_item<2>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+    const int gs = A.q_heads / A.kv_heads;
+    if (A.hd == 128) {
+      if (gs <= 4) attn_item<4, 4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+      else attn_item<4, kMaxGroup>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+    } else {
+      if (gs <= 4) attn_item<2, 4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+      else attn_item<2, kMaxGroup>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+    }
     __syncthreads();
   }
 }
@@ -708,7 +925,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   extern __shared__ __align__(128) unsigned char smem[];
   const StepHeader H = *img;
   const StepStage* stages = reinterpret_cast<const StepStage*>(img + 1);
-  unsigned* bar = reinterpret_cast<unsigned*>(ws + kWsBarrier);
+  unsigned* bar = reinterpret_cast<unsigned*>(ws + kWsFlags);
   unsigned* status = reinterpret_cast<unsigned*>(ws + kWsStatus);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (smem_u32(smem) != H.base) {  // the layout was planned for this base
@@ -726,10 +943,12 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   float* red = reinterpret_cast<float*>(smem + H.misc_off + kMiscRed);
   const uint16_t* cur_cb = nullptr;
   int cur_bits = 0;
+  if (H.nstages > 0 && stages[0].type == kLinear) stage_rs_prefetch(stages[0].lin, smem);
   for (int s = 0; s < H.nstages; ++s) {
     for (int i = tid; i < (int)(sizeof(StepStage) / 16); i += kStepThreads)
       reinterpret_cast<uint4*>(&st)[i] = reinterpret_cast<const uint4*>(&stages[s])[i];
     __syncthreads();
+    step_trace(s, 0);
     if (st.type == kLinear) {
       const LinearStage& L = st.lin;
       if (L.codebook != cur_cb || L.bits != cur_bits) {
@@ -742,17 +961,25 @@ __global__ void __launch_bounds__(kStepThreads, 1)
         cur_bits = L.bits;
         __syncthreads();
       }
-      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, ws, H);
-      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, ws, H);
-      else linear_stage<4>(L, smem, H.B, lut4, ws, H);
+      stage_prologue(L, smem, H.B, red);
+      step_trace(s, 1);
+      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, ws, H, s);
+      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, ws, H, s);
+      else linear_stage<4>(L, smem, H.B, lut4, ws, H, s);
     } else if (st.type == kAttention) {
       attn_stage(st.attn, H.B, pos, smem, ws, H);
     } else {
       final_norm_stage(st.fnorm, H.B, red);
     }
+    step_trace(s, 2);
     if (s + 1 == H.nstages) break;
-    if (stages[s + 1].type == kLinear) prefetch_stage(stages[s + 1].lin);
+    if (stages[s + 1].type == kLinear) {
+      __syncthreads();  // this stage's shared buffers are free
+      prefetch_stage(stages[s + 1].lin);
+      stage_rs_prefetch(stages[s + 1].lin, smem);
+    }
     if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x, s_ok)) break;
+    step_trace(s, 3);
   }
 }
 
@@ -816,49 +1043,65 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
   L.rt_total = rt;
   const int U = L.units_k;
   const int blk_units = std::max(1, static_cast<int>(f.block / kUnitCols));
-  // K-slices: the smallest count whose activations fit; slices are whole
-  // Hadamard blocks
-  const uint32_t cap_b = R.b1 - R.b0, cap_a = R.has4 ? 0 : R.a1 - R.a0;
-  int us = 0, kparts = 0, rpp = 0;
-  uint32_t z_need = 0, xs_need = 0;
+  // K-slices: the smallest count whose buffers fit; slices are whole
+  // Hadamard blocks.  Buffers go to region a (below the bits <= 3 table)
+  // first -- a small shared-memory footprint leaves the SM more L1 -- then
+  // to region b (after the table).
+  int us = 0, kparts = 0, rpp = 0, rs_smem = 1;
+  uint32_t off[4] = {0, 0, 0, 0};  // z, xin, scr, rs
   bool found = false;
-  for (kparts = 1; kparts <= U && !found; ++kparts) {
-    us = (U + kparts - 1) / kparts;
-    us = (us + blk_units - 1) / blk_units * blk_units;
-    const int kp = (U + us - 1) / us;
-    if (kp != kparts) continue;
-    const int cols = us * kUnitCols;
-    z_need = static_cast<uint32_t>(((int64_t)nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128);
-    for (rpp = B; rpp >= 1; --rpp) {
-      // xin (fp16) + FWHT scratch (fp32) for rpp rows
-      xs_need = static_cast<uint32_t>(((int64_t)rpp * cols * 2 + 127) / 128 * 128 + (int64_t)rpp * cols * 4);
-      const bool fit = R.has4 ? z_need + xs_need <= cap_b : (z_need <= cap_b && xs_need <= cap_a) ||
-                                                               (xs_need <= cap_b && z_need <= cap_a) ||
-                                                               z_need + xs_need <= cap_b;
-      if (fit) {
-        found = true;
-        break;
+  auto place = [&](const uint32_t* sz) {
+    uint32_t ua = 0, ub = 0;
+    const uint32_t ca = R.has4 ? 0 : R.a1 - R.a0, cb = R.b1 - R.b0;
+    for (int i = 0; i < 4; ++i) {
+      if (sz[i] == 0) {
+        off[i] = R.b0 - R.base;
+        continue;
+      }
+      if (ua + sz[i] <= ca) {
+        off[i] = R.a0 - R.base + ua;
+        ua += sz[i];
+      } else if (ub + sz[i] <= cb) {
+        off[i] = R.b0 - R.base + ub;
+        ub += sz[i];
+      } else {
+        return false;
       }
     }
-    if (found) break;
+    return true;
+  };
+  for (int attempt = 0; attempt < 2 && !found; ++attempt) {
+    rs_smem = attempt == 0 ? 1 : 0;
+    for (kparts = 1; kparts <= U && !found; ++kparts) {
+      us = (U + kparts - 1) / kparts;
+      us = (us + blk_units - 1) / blk_units * blk_units;
+      const int kp = (U + us - 1) / us;
+      if (kp != kparts) continue;
+      const int cols = us * kUnitCols;
+      const bool need_scr = !(rs_smem && L.lg_block <= 9);
+      for (rpp = B; rpp >= 1; --rpp) {
+        const uint32_t sz[4] = {
+            static_cast<uint32_t>(((int64_t)nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128),
+            static_cast<uint32_t>(((int64_t)rpp * cols * 2 + 127) / 128 * 128),
+            need_scr ? static_cast<uint32_t>((int64_t)rpp * cols * 4) : 0u,
+            static_cast<uint32_t>((int64_t)rs_smem * nops * cols * 2)};
+        if (place(sz)) {
+          found = true;
+          break;
+        }
+      }
+      if (found) break;
+    }
   }
   if (!found) return fail(TP_ERR_UNSUPPORTED, "tp_step: activations of d=%d do not fit shared memory", L.d);
+  L.rs_smem = rs_smem;
   L.kparts = kparts;
   L.us = us;
   L.rpp = rpp;
-  const int cols = us * kUnitCols;
-  const uint32_t xin_bytes = static_cast<uint32_t>(((int64_t)rpp * cols * 2 + 127) / 128 * 128);
-  if (!R.has4 && z_need <= cap_b && xs_need <= cap_a) {
-    L.z_off = R.b0 - R.base;
-    L.xin_off = R.a0 - R.base;
-  } else if (!R.has4 && xs_need <= cap_b && z_need <= cap_a) {
-    L.z_off = R.a0 - R.base;
-    L.xin_off = R.b0 - R.base;
-  } else {
-    L.z_off = R.b0 - R.base;
-    L.xin_off = R.b0 - R.base + z_need;
-  }
-  L.scr_off = L.xin_off + xin_bytes;
+  L.z_off = off[0];
+  L.xin_off = off[1];
+  L.scr_off = off[2];
+  L.rs_off = off[3];
   // grid split
   L.cps = std::max(1, G / kparts);
   const int64_t W = (int64_t)L.cps * kStepWarps;
@@ -921,6 +1164,7 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   cudaFuncAttributes fa{};
   TP_CUDA_TRY(cudaFuncGetAttributes(&fa, step_kernel), "cudaFuncGetAttributes(step)");
   const int G = step_sm_count();
+  if (G > kMaxGrid) return fail(TP_ERR_UNSUPPORTED, "tp_step: more than %d SMs", kMaxGrid);
   Regions R{};
   R.base = static_cast<uint32_t>((reserved + fa.sharedSizeBytes + 127) / 128 * 128);
   R.dyn_max = static_cast<uint32_t>(optin) - static_cast<uint32_t>(fa.sharedSizeBytes);
@@ -934,10 +1178,10 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   const uint32_t lut_end = has4 ? R.base + 131072u : kLutAbs + 65536u;
   if (!has4 && R.base > kLutAbs - 4096) return fail(TP_ERR_UNSUPPORTED, "tp_step: shared-memory base too high");
   R.a0 = R.base;
-  R.a1 = has4 ? R.base : kLutAbs;
-  R.b0 = lut_end + kMiscBytes;
+  R.a1 = has4 ? R.base : kLutAbs - kMiscBytes;
+  R.b0 = has4 ? lut_end + kMiscBytes : lut_end;
   R.b1 = R.base + R.dyn_max;
-  const uint32_t misc_off = lut_end - R.base;
+  const uint32_t misc_off = (has4 ? lut_end : kLutAbs - kMiscBytes) - R.base;
 
   // Codebooks are compared by value (read once here): layers whose
   // codebooks hold the same levels share one pointer, so the kernel rebuilds
@@ -976,11 +1220,13 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   uint16_t* ub = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(gb) + B * align256(m->inter) * 2 + 256);
   int64_t rt_max = 0, part_floats = 0;
   int ns = 0;
-  int nsplit = std::max(1, G / (B * m->kv_heads));
+  int nsplit = std::min(kMaxSplits, std::max(1, G / (B * m->kv_heads)));
   const int gs = m->q_heads / m->kv_heads;
   const uint32_t attn_buf = static_cast<uint32_t>(
       (kMaxGroup * hd + 2 * hd + kStepWarps * gs * (hd + 2)) * 4);
-  if (R.b0 + attn_buf > R.b1) return fail(TP_ERR_UNSUPPORTED, "tp_step: attention buffers do not fit");
+  const bool attn_in_a = !has4 && R.a0 + attn_buf <= R.a1;
+  const uint32_t attn_at = attn_in_a ? R.a0 : R.b0;
+  if (!attn_in_a && R.b0 + attn_buf > R.b1) return fail(TP_ERR_UNSUPPORTED, "tp_step: attention buffers do not fit");
   for (int i = 0; i < m->layers; ++i) {
     const tp_step_layer& ly = layers[i];
     if (!ly.ln1 || !ly.ln2 || !ly.k_cache || !ly.v_cache) return fail(TP_ERR_ARG, "tp_step: layer %d incomplete", i);
@@ -1022,7 +1268,7 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
       A.nsplit = nsplit;
       A.eps = m->rms_eps;
       A.scaling = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
-      A.buf_off = R.b0 - R.base;
+      A.buf_off = attn_at - R.base;
     }
     // O
     {
@@ -1070,16 +1316,21 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
     s.fnorm.d = m->hidden;
     s.fnorm.eps = m->rms_eps;
   }
-  // the largest linear-stage footprint sets the dynamic shared memory size
-  uint32_t end = std::max<uint32_t>(R.b0 + attn_buf, R.b0);
+  // the largest footprint over the stages sets the dynamic shared memory size
+  uint32_t end = std::max<uint32_t>(has4 ? R.b0 : kLutAbs + 65536u, attn_at + attn_buf);
   for (int s = 0; s < ns; ++s) {
     if (st[s].type != kLinear) continue;
     const LinearStage& L = st[s].lin;
     const int cols = L.us * kUnitCols;
-    const uint32_t zb = static_cast<uint32_t>(((int64_t)L.nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128);
-    const uint32_t xb = static_cast<uint32_t>(((int64_t)L.rpp * cols * 2 + 127) / 128 * 128 + (int64_t)L.rpp * cols * 4);
-    end = std::max(end, R.base + L.z_off + zb);
-    end = std::max(end, R.base + L.xin_off + xb);
+    const bool need_scr = !(L.rs_smem && L.lg_block <= 9);
+    const uint32_t sz[4] = {
+        static_cast<uint32_t>(((int64_t)L.nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128),
+        static_cast<uint32_t>(((int64_t)L.rpp * cols * 2 + 127) / 128 * 128),
+        need_scr ? static_cast<uint32_t>((int64_t)L.rpp * cols * 4) : 0u,
+        static_cast<uint32_t>((int64_t)L.rs_smem * L.nops * cols * 2)};
+    const uint32_t offs[4] = {L.z_off, L.xin_off, L.scr_off, L.rs_off};
+    for (int i = 0; i < 4; ++i)
+      if (sz[i]) end = std::max(end, R.base + offs[i] + sz[i]);
   }
   H->nstages = ns;
   H->B = B;
@@ -1113,14 +1364,23 @@ extern "C" tp_status tp_step_run(const void* image_dev, const void* image_host, 
   {
     std::lock_guard<std::mutex> lk(g_step_mu);
     if (dev < 0 || dev >= 64) return fail(TP_ERR_UNSUPPORTED, "device index out of range");
-    if (g_step_smem_set[dev] < (int)H->dyn) {
+    if (g_step_smem_set[dev] != (int)H->dyn) {
       TP_CUDA_TRY(cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)H->dyn),
                   "cudaFuncSetAttribute(step)");
+      // ask for the smallest shared-memory carve-out that holds the program,
+      // so the rest of the SM's on-chip memory serves as L1 (register spills
+      // and the noinline calls' saves stay on chip)
+      int smem_sm = 0;
+      TP_CUDA_TRY(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev), "attr");
+      const int pct = std::min(100, (int)(((int64_t)(H->dyn + H->base) * 100 + smem_sm - 1) / smem_sm));
+      TP_CUDA_TRY(cudaFuncSetAttribute(step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, pct),
+                  "cudaFuncSetAttribute(step carveout)");
       g_step_smem_set[dev] = (int)H->dyn;
     }
   }
   cudaStream_t st = as_stream(stream);
-  TP_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(workspace) + kWsBarrier, 0, 4, st), "memset(barrier)");
+  TP_CUDA_TRY(cudaMemsetAsync(static_cast<unsigned char*>(workspace) + kWsFlags, 0, 4 * kMaxGrid, st),
+              "memset(barrier words)");
   const StepHeader* img = static_cast<const StepHeader*>(image_dev);
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   void* args[] = {(void*)&img, (void*)&ws, (void*)&pos_dev};
@@ -1142,3 +1402,9 @@ extern "C" tp_status tp_step_status(const void* workspace, void* stream) {
   if (v & kStepStatusLayout) return fail(TP_ERR_DEVICE, "tp_step: shared-memory layout check failed (status %u)", v);
   return fail(TP_ERR_DEVICE, "tp_step: a grid barrier timed out (status %u)", v);
 }
+
+#ifdef TP_STEP_TRACE
+extern "C" TP_API int tp_step_trace_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, tp::g_step_trace, sizeof(tp::g_step_trace));
+}
+#endif
