@@ -1,33 +1,38 @@
 #!/usr/bin/env python
 """Benchmark of the packed-TCQ decode path on B200 (prints ONE JSON line).
 
-Workload (BASELINE metric "TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s,
-3-bit Qwen3-4B shape"): one step = one batch-1 decode pass through every
-packed linear of a Qwen3-4B-shaped decoder (36 layers x q/k/v/o/gate/up/down,
-3-bit packed TCQ, S = 64, per-layer rotation seeds).  The step runs two
-ways: as the persistent decode engine (every linear in one cooperative
-launch, tp_engine_run) and as per-layer tp_tcq_gemv calls, each captured in
-a CUDA graph; the faster is the headline, the other is reported beside it.  Weights are seeded random trellis streams (every bit string is a
-valid TCQ codeword) with the reference's data-free trellis codebook; the
-1.36 GB of packed weights exceed the 126 MB L2, so every step streams them
+Metric (BASELINE): "TCQ GEMV achieved HBM GB/s; batch-1 decode tok/s, 3-bit
+Qwen3-4B shape".  One step = one greedy batch-1 decode step of a
+Qwen3-4B-shaped decoder (36 layers, 3-bit packed TCQ, S = 64, random-init
+weights: seeded random trellis streams with the reference's data-free
+codebook) against a 1024-token synthetic KV cache: the whole-model step
+kernel (tp_step_run: norms, q/k/v, head norms, RoPE, KV append, GQA
+attention, o_proj, SiLU MLP, residuals, final norm) plus the greedy fp16 LM
+head (151936 x 2560, tp_lm_head_argmax) and the embedding row of the chosen
+token, replayed from a CUDA graph token after token.  The 1.37 GB of packed
+weights and 0.78 GB LM head exceed the 126 MB L2, so every step streams them
 from HBM.
 
-  value    = algorithmic bytes of all GEMVs of a step / device time of a step
-  e2e      = the same metric through the public module API with the step's
-             input copied from pinned host memory and the result read back
-  roofline = the headline path's kernels alone, timed with CUDA events
-             (the engine launch; or every fused GEMV in an instrumented
-             graph replay)
-  --impl reference : the reference path's CPU restatement (oracle port) on
-             the host cores, on bounded samples of the same workload.
+  value    = algorithmic bytes of a step (packed weights + scales / codebooks
+             / rotation scales, KV cache read + append, LM head, activations)
+             / device time of a step
+  tok_s    = batch * steps per second
+  e2e      = the same step through the public API (DecodeStep + GreedyLMHead)
+             with each step's token ids copied in from pinned host memory
+             and the chosen tokens read back
+  roofline = the step kernel alone (CUDA events around tp_step_run), its
+             algorithmic bytes over its duration, against MEASURED_PEAKS.json
+  gemv_c3  = the standalone packed GEMV (Llama-3-8B shapes x
+             2/3/4 bits x batch 1/4/16) with an oracle spot check per shape
+  c1       = BASELINE config 1 (1024 x 1024, 2-bit): the GPU GEMV and the
+             reference's own CPU forward (tiled and cached) on this host
+  decode_c4 = BASELINE config 4: mixed 2/3/4-bit Qwen3-4B at batch 1 and 8
+  cpu_baseline / --impl reference : the reference's CPU tiled forward
+             restated in torch (oracle/torch_cpu.py), all host threads.
 
-Under torchrun (N > 1) every rank first runs the tensor-parallel engine (each
-linear row-sharded over the N GPUs, outputs exchanged over NVLink inside the
-kernel) and reports it under "tp"; the line's value then comes from N
-replicas, each GPU decoding its own batch-1 stream with the whole model
-(scaling "weak"), which is how a 4B model is served on N GPUs.
---parallel tp makes the tensor-parallel step the line itself (the
-Llama-3-70B-shaped configuration: --model llama3-70b --bits 2).
+Under torchrun (N > 1) every rank decodes its own batch-1 stream with the
+whole model (replicas, scaling "weak"); the tensor-parallel engine of the
+decoder linears is reported under "tp" (--parallel tp makes it the line).
 """
 
 from __future__ import annotations
@@ -201,25 +206,51 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline_sample(cfg: dict, bits: int, which: list[int], seed: int = 0) -> tuple[float, int, float]:
-    """Time the oracle port (CPU restatement of the reference tiled forward)
-    on a sample of the workload's linears.  Returns (GB/s, bytes, seconds)."""
-    from oracle import tcq_oracle as O
+def cpu_info() -> dict:
+    import torch
 
-    shapes = linear_shapes(cfg)
+    model = ""
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": model}
+
+
+def cpu_layer_sample(cfg: dict, bits: int, which: list[int], seed: int = 0, cached: bool = False,
+                     tile_rows: int = 1024) -> tuple[int, float]:
+    """Time the reference's CPU forward (torch restatement, oracle/torch_cpu.py;
+    tiled, or cached = decode once then F.linear) over linears of one decoder
+    layer.  Returns (packed bytes, seconds)."""
+    import torch
+
+    from oracle import tcq_oracle as O
+    from oracle import torch_cpu as T
+
+    torch.set_num_threads(os.cpu_count() or 1)
     cb = codebook(bits)
-    total_b, total_t = 0, 0.0
+    shapes = linear_shapes(cfg)
+    tot_b, tot_t = 0, 0.0
     rng = np.random.default_rng(seed)
     for idx in which:
         name, d, n = shapes[idx % len(shapes)]
         p = O.random_payload(n, d, bits, 64, seed=layer_seed(seed, 0, name), codebook=cb)
-        x = rng.standard_normal((1, d)).astype(np.float16)
-        t0 = time.perf_counter()
-        O.forward_fp32(p, x)
-        total_t += time.perf_counter() - t0
-        total_b += gemv_bytes(n, d, bits, 1)
-    return total_b / total_t / 1e9, total_b, total_t
-
+        x = torch.from_numpy(rng.standard_normal((1, d)).astype(np.float16))
+        with torch.no_grad():
+            if cached:
+                w16 = T.cached_weight(p)
+                t0 = time.perf_counter()
+                T.cached_forward(w16, x)
+            else:
+                rs = T.rot_scale(p)
+                t0 = time.perf_counter()
+                T.tiled_forward(p, x, rs, tile_rows)
+        tot_t += time.perf_counter() - t0
+        tot_b += gemv_bytes(n, d, bits, 1)
+    return tot_b, tot_t
 
 def peaks_hbm() -> tuple[float, str]:
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -354,8 +385,124 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
 
 
 
-def run_gpu(args) -> dict | None:
+def codebooks_t() -> dict:
     import torch
+
+    return {b: torch.from_numpy(codebook(b)) for b in (2, 3, 4)}
+
+
+def build_step(cfg: dict, layer_bits: list[int], B: int, dev, seed: int, ctx: int, max_tokens: int,
+               layers=None, head=None):
+    """DecodeStep over a synthetic decoder, its tied fp16 embedding / LM head
+    matrix and an N(0,1) KV cache of `ctx` positions."""
+    import torch
+
+    from turbopress_b200.step import DecodeStep
+    from turbopress_b200.synthetic import step_config, synthetic_decoder
+
+    if layers is None:
+        layers, fnorm = synthetic_decoder(cfg, layer_bits, codebooks_t(), dev, seed=seed)
+    else:
+        layers, fnorm = layers
+    g = torch.Generator(device=dev).manual_seed(seed + 7)
+    if head is None:
+        head = (torch.randn(cfg["vocab"], cfg["hidden"], generator=g, device=dev) * 0.02).half()
+    step = DecodeStep(layers, step_config(cfg), fnorm, batch=B, max_tokens=max_tokens, lm_head=head)
+    step.k_cache[:, :, :, :ctx].normal_(generator=g)
+    step.v_cache[:, :, :, :ctx].normal_(generator=g)
+    step.set_position(ctx)
+    return step, (layers, fnorm), head
+
+
+def step_bytes_total(step, cfg: dict, B: int, ctx: int) -> tuple[int, int]:
+    """(step-kernel algorithmic bytes, whole-step bytes incl. LM head and the
+    embedding rows)."""
+    from turbopress_b200.step import step_algorithmic_bytes
+
+    kb = step_algorithmic_bytes(step.layers, step.cfg, B, ctx)
+    kb += 2 * B * cfg["hidden"] * 2 + 2 * cfg["hidden"]  # final norm in/out + weight
+    head = 2 * cfg["vocab"] * cfg["hidden"] + 2 * B * cfg["hidden"] + 12 * B
+    return kb, kb + head + 2 * B * cfg["hidden"]
+
+
+def time_decode(step, head, B: int, ctx: int, steps: int, warmup: int, stream, local: int, with_clocks=True):
+    """Greedy decode steps replayed from a CUDA graph: device ms per step,
+    kernel-only ms of tp_step_run, e2e ms per step, clocks."""
+    import torch
+
+    dev = step.device
+    tok = torch.zeros(B, dtype=torch.int64, device=dev)
+    # everything built on the default stream (weights, caches, tok) is ready
+    # before the side stream uses it
+    stream.wait_stream(torch.cuda.current_stream(dev))
+
+    V = head.shape[0]
+
+    def one_token():
+        # token ids are clamped into the vocabulary before the lookup
+        step.hidden.copy_(head.index_select(0, tok.clamp(0, V - 1)))
+        out = step.run()
+        nxt, _ = step.lm_head(out)
+        step.advance()
+        tok.copy_(nxt)
+
+    with torch.cuda.stream(stream):
+        one_token()
+        stream.synchronize()
+        step.status()
+        t0 = tok.cpu()
+        if int(t0.min()) < 0 or int(t0.max()) >= V or not bool(torch.isfinite(step.final_out).all()):
+            raise RuntimeError(f"decode step produced token ids {t0.tolist()} (vocabulary {V}) / non-finite output")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            one_token()
+        step.set_position(ctx)
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        step.set_position(ctx)
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(local) if with_clocks else None
+        if clk:
+            clk.__enter__()
+        a.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        b.record(stream)
+        b.synchronize()
+        if clk:
+            clk.__exit__(None, None, None)
+        ms = a.elapsed_time(b) / steps
+        # the step kernel alone
+        step.set_position(ctx)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(steps):
+            step.run()
+        k1.record(stream)
+        k1.synchronize()
+        ms_kernel = k0.elapsed_time(k1) / steps
+        step.status()
+        # end to end: token ids in from pinned host memory, chosen tokens out
+        step.set_position(ctx)
+        t_in = torch.zeros(B, dtype=torch.int64).pin_memory()
+        t_out = torch.zeros(B, dtype=torch.int64).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            tok.copy_(t_in, non_blocking=True)
+            graph.replay()
+            t_out.copy_(tok, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / steps
+    return ms, ms_kernel, ms_e2e, (clk.summary() if clk else None), int(t_in.numel() * 8), int(t_out.numel() * 8)
+
+
+def run_decode(args) -> dict | None:
+    import torch
+
+    from turbopress_b200.synthetic import MODELS as SMODELS, mixed_bits
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -372,239 +519,231 @@ def run_gpu(args) -> dict | None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    cfg, bits, B = dict(MODELS[args.model]), args.bits, args.batch
-    if args.layers:
-        cfg["layers"] = args.layers  # profiling of a small case only
+    cfg = dict(SMODELS[args.model])
+    B, bits = args.batch, args.bits
     tp_line = None
     if world > 1:
-        # tensor parallel: one model split over the ranks (latency of one stream)
-        tp_line = run_tp(args, cfg, rank, world, local, dev, dist)
+        # tensor-parallel engine of the decoder linears (one stream over N GPUs)
+        tp_line = run_tp(args, dict(MODELS[args.model]), rank, world, local, dev, dist)
         if args.parallel == "tp":
             dist.destroy_process_group()
             return tp_line
-        # replicas: every rank decodes its own batch-1 stream with the whole model
-    mods = build_model(cfg, bits, dev, seed=args.seed)
-    step_bytes = sum(gemv_bytes(n, d, bits, B) for _ in range(cfg["layers"]) for _, d, n in linear_shapes(cfg))
-    n_gemv = cfg["layers"] * len(LINEARS)
-    launches_per_gemv = 2 * math.ceil(B / 32)  # rotation + fused GEMV per batch chunk of 32
-
-    x_static = torch.randn(B, cfg["hidden"], device=dev, dtype=torch.float16)
+    ctx = 1024 if args.model == "qwen3-4b" else 512 if args.model == "qwen3-0.6b" else 2048
+    layer_bits = [bits] * cfg["layers"]
+    steps, warm = args.steps, max(args.warmup, 3)
+    max_tok = ctx + 3 * steps + warm + 16
     stream = torch.cuda.Stream(device=dev)
-    stream.wait_stream(torch.cuda.current_stream())
-    with torch.no_grad(), torch.cuda.stream(stream):
-        for _ in range(3):
-            decode_step(mods, x_static, cfg["layers"])
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            y_static = decode_step(mods, x_static, cfg["layers"])
-        # instrumented graph: events around every packed linear
-        ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-              for _ in range(n_gemv)]
-        gbytes = [gemv_bytes(n, d, bits, B) for _ in range(cfg["layers"]) for _, d, n in linear_shapes(cfg)]
-        graph_i = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph_i, stream=stream):
-            h = x_static
-            it = iter(range(n_gemv))
-            for i in range(cfg["layers"]):
-                outs = []
-                for j, m in enumerate(mods[7 * i: 7 * i + 7]):
-                    inp = h if j in (0, 1, 2) else outs[3] if j in (4, 5) else outs[0] if j == 3 else outs[4]
-                    k = next(it)
-                    ev[k][0].record(stream)
-                    outs.append(m(inp))
-                    ev[k][1].record(stream)
-                h = outs[6]
-    torch.cuda.synchronize()
-
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            graph.replay()
-        barrier()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as clk:
-            start.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            end.record(stream)
-            end.synchronize()
-        barrier()
-        ms = start.elapsed_time(end) / args.steps
-
-        # per-launch durations of the fused GEMV (instrumented replay)
-        for _ in range(2):
-            graph_i.replay()
-        stream.synchronize()
-        durs = np.array([a.elapsed_time(b) for a, b in ev])  # ms
-        ach_gbs = float(np.sum(gbytes) / (np.sum(durs) * 1e-3) / 1e9)
-        per_shape = {}
-        for k, (name, d, n) in enumerate(linear_shapes(cfg)):
-            sel = durs[k::7]
-            per_shape[name] = {"us": round(float(np.mean(sel)) * 1e3, 2),
-                               "gbs": round(gemv_bytes(n, d, bits, B) / (float(np.mean(sel)) * 1e-3) / 1e9, 1)}
-
-        # end to end: pinned host input -> device, step, result -> pinned host
-        x_host = torch.randn(B, cfg["hidden"], dtype=torch.float16).pin_memory()
-        y_host = torch.empty(B, cfg["hidden"], dtype=torch.float16).pin_memory()
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            x_static.copy_(x_host, non_blocking=True)
-            graph.replay()
-            y_host.copy_(y_static, non_blocking=True)
-        e1.record(stream)
-        e1.synchronize()
-        ms_e2e = e0.elapsed_time(e1) / args.steps
-
-    # persistent engine: the same step as ONE cooperative launch
-    eng = None
-    if B <= 4 and not args.no_engine:
-        from turbopress_b200.engine import DecodeEngine
-        eng = DecodeEngine(mods, engine_inputs(cfg["layers"]), batch=B, input_dtype=torch.float16)
-        with torch.cuda.stream(stream):
-            eng.set_input(x_static)
-            eng.run()
-            stream.synchronize()
-            eng.check()
-            graph_e = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph_e, stream=stream):
-                eng.run()
-            for _ in range(max(args.warmup, 3)):
-                graph_e.replay()
-            barrier()
-            with ClockSampler(local) as clk_e:
-                es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                es.record(stream)
-                for _ in range(args.steps):
-                    graph_e.replay()
-                ee.record(stream)
-                ee.synchronize()
-            barrier()
-            ms_eng = es.elapsed_time(ee) / args.steps
-            # the engine kernel alone (outputs zeroed outside the events)
-            kd = []
-            for _ in range(3):
-                eng.y_arena.zero_()
-                eng.counters.zero_()
-                k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                k0.record(stream)
-                eng.launch()
-                k1.record(stream)
-                k1.synchronize()
-                kd.append(k0.elapsed_time(k1))
-            eng.check()
-            ms_kernel = float(np.median(kd))
-            # end to end through the engine: pinned host in, graph, fp32 result out
-            y32_host = torch.empty(B, cfg["hidden"], dtype=torch.float32).pin_memory()
-            xin = eng.x_ext[cfg["hidden"]]
-            barrier()
-            e0.record(stream)
-            for _ in range(args.steps):
-                xin.copy_(x_host, non_blocking=True)
-                graph_e.replay()
-                y32_host.copy_(eng.outputs[-1], non_blocking=True)
-            e1.record(stream)
-            e1.synchronize()
-            ms_eng_e2e = e0.elapsed_time(e1) / args.steps
-    else:
-        ms_eng = ms_kernel = ms_eng_e2e = float("inf")
-
-    t = torch.tensor([ms, ms_e2e, ms_eng, ms_eng_e2e, ms_kernel], device=dev)
+    step, parts, head = build_step(cfg, layer_bits, B, dev, args.seed, ctx, max_tok)
+    barrier()
+    ms, ms_kernel, ms_e2e, clocks, h2d, d2h = time_decode(step, head, B, ctx, steps, warm, stream, local)
+    kbytes, sbytes = step_bytes_total(step, cfg, B, ctx)
+    extra = {}
+    if world == 1 and not args.quick:
+        # mixed 2/3/4-bit layers, batch 1 and 8
+        mb = mixed_bits(cfg["layers"], seed=args.seed)
+        del step
+        torch.cuda.empty_cache()
+        c4 = {"bits_per_layer": mb, "avg_bits": sum(mb) / len(mb)}
+        shared = None
+        for b in (1, 8):
+            st, shared, _ = build_step(cfg, mb, b, dev, args.seed + 1, ctx, max_tok, layers=shared, head=head)
+            m, mk, me, _, _, _ = time_decode(st, head, b, ctx, steps, warm, stream, local, with_clocks=False)
+            kb, sb = step_bytes_total(st, cfg, b, ctx)
+            c4[f"batch{b}"] = {"ms_per_step": round(m, 4), "tok_s": round(b * 1000.0 / m, 1),
+                              "kernel_ms": round(mk, 4), "gbs": round(sb / (m * 1e-3) / 1e9, 1),
+                              "e2e_tok_s": round(b * 1000.0 / me, 1)}
+            del st
+            torch.cuda.empty_cache()
+        extra["decode_c4"] = c4
+        del shared
+        torch.cuda.empty_cache()
+    t = torch.tensor([ms, ms_e2e, ms_kernel], device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_eng, ms_eng_e2e, ms_kernel = (float(v) for v in t)
+    ms, ms_e2e, ms_kernel = (float(v) for v in t)
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
         return None
-
-    peaks = {}
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peaks = json.loads(pk.read_text())
-    peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    use_engine = ms_eng < ms
-    ms_head = ms_eng if use_engine else ms
-    ms_head_e2e = ms_eng_e2e if use_engine else ms_e2e
-    value = world * step_bytes / (ms_head * 1e-3) / 1e9
-    graph_line = {"ms_per_step": round(ms, 4), "value": round(world * step_bytes / (ms * 1e-3) / 1e9, 1),
-                  "tok_s": round(world * B * 1000.0 / ms, 1),
-                  "e2e_tok_s": round(world * B * 1000.0 / ms_e2e, 1),
-                  "gemv_achieved_gbs": round(ach_gbs, 1), "per_shape": per_shape,
-                  "launches_per_step": n_gemv * launches_per_gemv}
-    if use_engine:
-        ach = step_bytes / (ms_kernel * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(ach / peak, 4),
-                "traffic": round(step_bytes * TRAFFIC_RATIO) if TRAFFIC_RATIO else None,
-                "kernel": "tcq_engine_kernel (one cooperative launch per step, all 252 GEMVs), "
-                          "algorithmic bytes of the step / median CUDA-event duration of the launch",
-                "kernel_ms": round(ms_kernel, 4),
-                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
-                else "fallback 6650 GB/s"}
-        launches = args.steps
-        path = "persistent engine (tp_engine_run), CUDA graph"
-    else:
-        roof = {"bound": "hbm", "achieved": round(ach_gbs, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(ach_gbs / peak, 4), "traffic": None,
-                "kernel": "tp_tcq_gemv (rotation + fused decode-GEMV launches), mean over the step's 252 GEMVs",
-                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
-                else "fallback 6650 GB/s", "per_shape": per_shape}
-        launches = args.steps * n_gemv * launches_per_gemv
-        path = "per-layer tp_tcq_gemv calls, CUDA graph"
+    peak, peak_src = peaks_hbm()
+    ach = kbytes / (ms_kernel * 1e-3) / 1e9
     out = {
-        "metric": metric_name(cfg, bits),
-        "value": round(value, 1),
+        "metric": metric_name(MODELS[args.model], bits),
+        "value": round(world * sbytes / (ms * 1e-3) / 1e9, 1),
         "unit": "GB/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": max(args.warmup, 3),
-        "ms_per_step": round(ms_head, 4),
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": round(ms, 4),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": f"u8 packed TCQ ({bits} bits/weight) -> fp16 activations, fp32 accumulate",
-        "data": "synthetic: seeded random trellis streams + reference data-free codebook; x N(0,1) fp16",
-        "config": {"workload": f"{cfg['name']} decoder linears, batch {B}, {bits}-bit packed TCQ, S=64",
-                   "path": path,
-                   "layers": cfg["layers"], "linears_per_step": n_gemv, "batch": B, "bits": bits,
-                   "weights_bytes_per_step": int(step_bytes),
-                   "l2": "inputs larger than L2 (packed weights per step > 126 MB L2)",
+        "data": "synthetic: random-init decoder (seeded random trellis streams + reference data-free codebook, "
+                "norm weights 1+N(0,0.1^2), fp16 LM head N(0,0.02^2)), KV cache N(0,1)",
+        "config": {"workload": f"{cfg['name']} greedy decode step, batch {B}, {bits}-bit packed TCQ (S=64), "
+                               f"{ctx}-token KV cache, LM head {cfg['vocab']}x{cfg['hidden']} fp16",
+                   "path": "tp_step_run (one cooperative launch per step) + tp_lm_head_argmax, CUDA graph",
+                   "layers": cfg["layers"], "batch": B, "bits": bits, "kv_tokens": ctx,
+                   "step_bytes": int(sbytes), "step_kernel_bytes": int(kbytes),
+                   "l2": "inputs larger than L2 (packed weights + LM head per step > 126 MB L2)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-        "tok_s": round(world * B * 1000.0 / ms_head, 1),
-        "e2e": {"value": round(world * step_bytes / (ms_head_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "tok_s": round(world * B * 1000.0 / ms_head_e2e, 1),
-                "h2d_bytes_per_step": int(x_host.numel() * 2),
-                "d2h_bytes_per_step": int(B * cfg["hidden"] * (4 if use_engine else 2))},
-        "gpu_launches": int(launches),
-        "roofline": roof,
-        "clocks": (clk_e if use_engine else clk).summary(),
-        "per_layer_graph": graph_line,
+        "tok_s": round(world * B * 1000.0 / ms, 1),
+        "e2e": {"value": round(world * sbytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "tok_s": round(world * B * 1000.0 / ms_e2e, 1), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(2 * steps),
+        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach / peak, 4), "traffic": None,
+                     "kernel": "step_kernel (tp_step_run): step-kernel algorithmic bytes / CUDA-event duration, "
+                               "mean over the timed launches",
+                     "kernel_ms": round(ms_kernel, 4), "peak_source": peak_src},
+        "clocks": clocks,
     }
-    if ms_eng != float("inf"):
-        out["engine"] = {"ms_per_step": round(ms_eng, 4), "kernel_ms": round(ms_kernel, 4),
-                         "value": round(world * step_bytes / (ms_eng * 1e-3) / 1e9, 1),
-                         "tok_s": round(world * B * 1000.0 / ms_eng, 1),
-                         "e2e_tok_s": round(world * B * 1000.0 / ms_eng_e2e, 1)}
+    out.update(extra)
     if tp_line is not None:
         out["tp"] = {"parallelism": f"tp{world}", "ms_per_step": tp_line["ms_per_step"], "tok_s": tp_line["tok_s"],
                      "value": tp_line["value"], "unit": "GB/s", "e2e_tok_s": tp_line["e2e"]["tok_s"],
                      "kernel_ms": tp_line["roofline"]["kernel_ms"], "roofline_frac": tp_line["roofline"]["frac"],
-                     "path": tp_line["config"]["path"]}
+                     "path": tp_line["config"]["path"], "workload": "decoder linears only (no attention)"}
+    if world == 1 and not args.quick:
+        out["gemv_c3"] = gemv_table(args, dev)
+        out["c1"] = c1_section(args, dev)
     if not args.no_cpu_baseline and world == 1:
-        gbs, nbytes, secs = cpu_baseline_sample(cfg, bits, list(range(7)), seed=args.seed)
-        out["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                               "sample": f"oracle forward of one decoder layer (7 linears, {nbytes / 1e6:.1f} MB "
-                                         f"packed) in {secs:.1f} s",
-                               "tok_s_extrapolated": round(1.0 / (secs * cfg["layers"]), 5)}
+        info = cpu_info()
+        nb, secs = cpu_layer_sample(dict(MODELS[args.model]), bits, list(range(7)), seed=args.seed)
+        nbc, secc = cpu_layer_sample(dict(MODELS[args.model]), bits, list(range(7)), seed=args.seed, cached=True)
+        out["cpu_baseline"] = {
+            "value": round(nb / secs / 1e9, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
+            "sample": f"reference tiled forward (torch restatement, oracle/torch_cpu.py) of one {cfg['name']} "
+                      f"decoder layer's 7 linears ({nb / 1e6:.1f} MB packed) in {secs:.2f} s",
+            "ms_per_mweight": round(secs * 1e3 / (sum(n * d for _, d, n in linear_shapes(MODELS[args.model])) / 1e6),
+                                    3),
+            "tok_s_extrapolated": round(1.0 / (secs * cfg["layers"]), 4),
+            "cached_tok_s_extrapolated": round(1.0 / (secc * cfg["layers"]), 4),
+            **info}
     if dist is not None:
         dist.destroy_process_group()
     return out
 
+
+def host_payload(n: int, d: int, bits: int, seed: int) -> dict:
+    """A format-v2 payload of uniform random packed bits (every bit string is
+    a valid trellis codeword) with the reference's data-free codebook."""
+    rng = np.random.default_rng(seed)
+    return {"format": 2, "n": n, "d": d, "bits": bits, "n_states": 64, "block": d & -d, "seed": seed,
+            "path_packed": rng.integers(0, 256, (n, -(-d // 8)), dtype=np.uint8),
+            "member_packed": rng.integers(0, 256, (n, -(-d * (bits - 1) // 8)), dtype=np.uint8) if bits > 1 else None,
+            "scales": ((rng.random(n) * 0.5 + 0.75) / math.sqrt(d)).astype(np.float16),
+            "signs_packed": rng.integers(0, 256, (1, -(-d // 8)), dtype=np.uint8),
+            "inv_equil": (rng.random(d) * 0.4 + 0.8).astype(np.float16),
+            "codebook": codebook(bits).astype(np.float16), "bias": None}
+
+
+def gemv_table(args, dev) -> dict:
+    """Llama-3-8B linear shapes x 2/3/4 bits x batch 1/4/16,
+    each GEMV in a CUDA graph of distinct weight copies (> 2x L2 in total),
+    GB/s and fraction of measured HBM peak, and an oracle spot check."""
+    import torch
+
+    from oracle import tcq_oracle as O
+
+    peak, _ = peaks_hbm()
+    res = {}
+    for n, d in ((4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)):
+        for bits in (2, 3, 4):
+            nbytes1 = n * d * bits // 8
+            copies = max(2, min(16, math.ceil(3 * 126e6 / nbytes1)))
+            # copy 0 from a host payload (kept for the oracle spot check), the rest generated on the GPU
+            from turbopress_b200 import PackedTCQLinear
+            p0 = host_payload(n, d, bits, seed=1000 * bits)
+            mods = [PackedTCQLinear({k: (torch.from_numpy(v).to(dev) if isinstance(v, np.ndarray) else v)
+                                     for k, v in p0.items()}, mode="cuda")]
+            mods += [random_linear(n, d, bits, dev, seed=1000 * bits + c) for c in range(1, copies)]
+            for B in (1, 4, 16):
+                x = torch.randn(B, d, device=dev, dtype=torch.float16)
+                s = torch.cuda.Stream(device=dev)
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.no_grad(), torch.cuda.stream(s):
+                    ys = [m(x) for m in mods]
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=s):
+                        for m in mods:
+                            m(x)
+                    for _ in range(3):
+                        graph.replay()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    reps = 10
+                    e0.record(s)
+                    for _ in range(reps):
+                        graph.replay()
+                    e1.record(s)
+                    e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps / copies
+                gb = gemv_bytes(n, d, bits, B) / (us * 1e-6) / 1e9
+                # oracle spot check: the first 32 rows of copy 0
+                p = dict(p0, n=32, path_packed=p0["path_packed"][:32], scales=p0["scales"][:32],
+                         member_packed=None if p0["member_packed"] is None else p0["member_packed"][:32])
+                ref = O.forward_fp32(p, x.cpu().numpy())
+                got = ys[0][:, :32].float().cpu().numpy()
+                rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+                res[f"{n}x{d}_b{bits}_B{B}"] = {"us": round(us, 2), "GBps": round(gb, 1),
+                                                 "frac": round(gb / peak, 4), "spot_rows": 32,
+                                                 "spot_rel_l2": float(f"{rel:.3e}")}
+                del graph, ys
+            del mods
+            torch.cuda.empty_cache()
+    return res
+
+
+def c1_section(args, dev) -> dict:
+    """BASELINE config 1 (the reference's CPU-runnable case): 1024 x 1024
+    2-bit, from the reference encoder (golden fixture).  GPU: the packed GEMV
+    (one layer, L2-resident); CPU: the reference tiled and cached forwards."""
+    import torch
+
+    from oracle import torch_cpu as T
+    from tests.conftest import load_golden, payload_from
+    from turbopress_b200 import PackedTCQLinear
+
+    g = load_golden("layers")
+    p = payload_from(g, "c1_")
+    x = g["c1_x"]
+    pd = {k: (torch.from_numpy(v).to(dev) if isinstance(v, np.ndarray) else v) for k, v in p.items()}
+    m = PackedTCQLinear(pd, mode="cuda")
+    xd = torch.from_numpy(x).to(dev)
+    with torch.no_grad():
+        y = m(xd)
+        for _ in range(10):
+            m(xd)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(100):
+            m(xd)
+        b.record()
+        b.synchronize()
+    us_gpu = a.elapsed_time(b) * 10.0
+    rel = float(np.linalg.norm(y.float().cpu().numpy() - g["c1_y_tiled"]) / np.linalg.norm(g["c1_y_tiled"]))
+    torch.set_num_threads(os.cpu_count() or 1)
+    xt = torch.from_numpy(x)
+    rs = T.rot_scale(p)
+    T.tiled_forward(p, xt, rs)
+    t0 = time.perf_counter()
+    for _ in range(5):
+        T.tiled_forward(p, xt, rs)
+    ms_tiled = (time.perf_counter() - t0) / 5 * 1e3
+    w16 = T.cached_weight(p)
+    T.cached_forward(w16, xt)
+    t0 = time.perf_counter()
+    for _ in range(50):
+        T.cached_forward(w16, xt)
+    ms_cached = (time.perf_counter() - t0) / 50 * 1e3
+    return {"shape": "1024x1024", "bits": 2, "gpu_us_per_call": round(us_gpu, 2),
+            "gpu_rel_l2_vs_reference_tiled": float(f"{rel:.3e}"),
+            "cpu_tiled_ms": round(ms_tiled, 3), "cpu_cached_ms": round(ms_cached, 4),
+            "cpu_threads": torch.get_num_threads(),
+            "note": "GPU time is per-call latency (the 0.26 MB layer is L2-resident)"}
 
 def random_linear(n: int, d: int, bits: int, device, seed: int, cb=None):
     """One PackedTCQLinear with seeded random trellis streams (GPU-generated)."""
@@ -630,49 +769,22 @@ def random_linear(n: int, d: int, bits: int, device, seed: int, cb=None):
 
 
 def run_gemv(args) -> dict:
-    """Standalone packed GEMVs (BASELINE config 3 shapes by default): per shape,
-    `copies` distinct weight sets in one CUDA graph (so each launch streams its
-    weights from HBM), timed with CUDA events; --once runs one call per shape
-    (for profiler captures)."""
+    """Standalone packed GEMVs: the BASELINE config 3 table, or with --once
+    one call per --shapes entry at --bits / --batch (for profiler captures)."""
     import torch
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    res = {}
+    if not args.once:
+        return {"workload": "gemv", "gemv_c3": gemv_table(args, dev)}
     for shp in args.shapes.split(","):
         n, d = map(int, shp.lower().split("x"))
-        copies = 1 if args.once else max(1, min(args.copies, int(2e9 // max(1, n * d * args.bits // 8))))
-        mods = [random_linear(n, d, args.bits, dev, seed=c) for c in range(copies)]
+        m = random_linear(n, d, args.bits, dev, seed=1)
         x = torch.randn(args.batch, d, device=dev, dtype=torch.float16)
-        if args.once:
-            mods[0](x)
-            torch.cuda.synchronize()
-            continue
-        s = torch.cuda.Stream(device=dev)
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.no_grad(), torch.cuda.stream(s):
-            for m in mods:
-                m(x)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=s):
-                for m in mods:
-                    m(x)
-            for _ in range(max(args.warmup, 3)):
-                graph.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(s)
-            for _ in range(args.steps):
-                graph.replay()
-            e1.record(s)
-            e1.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / args.steps / copies
-        nbytes = gemv_bytes(n, d, args.bits, args.batch)
-        res[shp] = {"us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1), "MB": round(nbytes / 1e6, 2),
-                    "TFLOPs": round(2 * args.batch * n * d / us / 1e6, 2), "copies": copies}
-        del mods, graph
-        torch.cuda.empty_cache()
-    return {"workload": "gemv", "bits": args.bits, "batch": args.batch, "shapes": res}
-
+        with torch.no_grad():
+            m(x)
+        torch.cuda.synchronize()
+    return {"workload": "gemv", "once": args.shapes, "bits": args.bits, "batch": args.batch}
 
 def run_lmhead(args) -> dict:
     """Greedy LM head (fp16 vocabulary GEMV + argmax), Qwen3 vocabulary x the
@@ -712,35 +824,38 @@ def run_lmhead(args) -> dict:
 
 
 def run_reference(args) -> dict | None:
+    """The reference arm: the reference's own CPU forward (tiled; torch
+    restatement in oracle/torch_cpu.py) on this host's cores, one linear of
+    the workload's decoder layer per step (cycling q/k/v/o/gate/up/down)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
     cfg, bits = dict(MODELS[args.model]), args.bits
     for i in range(args.warmup):
-        cpu_baseline_sample(cfg, bits, [i], seed=args.seed)
-    vals, tot_b, tot_t = [], 0, 0.0
+        cpu_layer_sample(cfg, bits, [i], seed=args.seed)
+    tot_b, tot_t = 0, 0.0
     for i in range(args.steps):
-        gbs, b, t = cpu_baseline_sample(cfg, bits, [i], seed=args.seed)
-        vals.append(gbs)
+        b, t = cpu_layer_sample(cfg, bits, [i], seed=args.seed)
         tot_b += b
         tot_t += t
     value = tot_b / tot_t / 1e9
-    ms = tot_t / args.steps * 1e3
+    info = cpu_info()
     return {
         "impl": "reference",
         "metric": metric_name(cfg, bits),
         "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u8 packed TCQ -> fp32 (reference CPU path)",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_t / args.steps * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u8 packed TCQ -> fp32 (reference CPU tiled path)",
         "data": "synthetic: seeded random trellis streams + reference data-free codebook",
         "config": {"workload": f"{cfg['name']} decoder linears, batch 1, {bits}-bit packed TCQ, S=64",
                    "sample": "one linear per step, cycling q/k/v/o/gate/up/down"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "oracle port of the reference tiled forward (unpack, window decode, fp16 "
-                                   "dequant, fp32 matmul), one linear per step"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
+                         "sample": "reference tiled forward (torch restatement of turbopress/runtime.py:291-331: "
+                                   "unpack, window decode, fp16 dequant per 1024-row tile, fp32 matmul), one "
+                                   "linear per step", **info},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-
 
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -752,31 +867,30 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="decode line only (no gemv_c3 / c1 / decode_c4 keys)")
     ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-4b",
                     help="decode workload: model shape (qwen3-4b is the contract line)")
     ap.add_argument("--parallel", choices=["replicas", "tp"], default="replicas",
-                    help="N > 1: the JSON line's value from N independent batch-1 streams (replicas, with the "
-                         "tensor-parallel step reported under 'tp') or from the tensor-parallel step itself")
-    ap.add_argument("--layers", type=int, default=0, help="decoder layers (default: the model's 36; "
-                    "smaller values are for ncu captures, not bench lines)")
-    ap.add_argument("--no-engine", action="store_true", help="decode workload: per-layer graph only")
+                    help="N > 1: the line from N independent decode streams (replicas, with the tensor-parallel "
+                         "engine of the decoder linears under 'tp') or the tensor-parallel engine itself")
+    ap.add_argument("--layers", type=int, default=0, help="tensor-parallel engine: decoder layers (profiling)")
     ap.add_argument("--workload", choices=["decode", "gemv", "lmhead"], default="decode",
-                    help="decode: the contract line (Qwen3-4B decode step); gemv: standalone GEMV table")
-    ap.add_argument("--shapes", default="14336x4096,4096x14336,4096x4096,1024x4096",
-                    help="gemv workload: comma-separated NxD (out x in) shapes")
-    ap.add_argument("--copies", type=int, default=16, help="gemv workload: distinct weight sets per shape")
+                    help="decode: the contract line; gemv: the config-3 GEMV table; lmhead: the greedy LM head")
+    ap.add_argument("--shapes", default="14336x4096", help="gemv --once: comma-separated NxD (out x in) shapes")
     ap.add_argument("--once", action="store_true", help="gemv workload: one call per shape (profiling)")
     args = ap.parse_args()
-    if args.workload == "lmhead" and args.impl != "reference":
-        print(json.dumps(run_lmhead(args)), flush=True)
-        return
-    if args.workload == "gemv" and args.impl != "reference":
-        print(json.dumps(run_gemv(args)), flush=True)
-        return
-    out = run_reference(args) if args.impl == "reference" else run_gpu(args)
+    if args.impl == "reference":
+        out = run_reference(args)
+    elif args.workload == "lmhead":
+        out = run_lmhead(args)
+    elif args.workload == "gemv":
+        out = run_gemv(args)
+    else:
+        out = run_decode(args)
     if out is not None:
         print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":
     main()
+

@@ -306,8 +306,14 @@ def random_payload(n: int, d: int, bits: int, n_states: int = 64, seed: int = 0,
 def lm_head_argmax(x: np.ndarray, w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """Greedy next token of the reference's decode loops: fp16 lm_head
     logits then ``logits[:, -1:].argmax(-1)`` (scripts/run_packed.py:164,178,190;
-    scripts/graph_decode_bench.py:55-112), with the logits in float64.
-    Returns (token index per batch row, logits [B, V]); np.argmax keeps the
-    first index among equal logits, as torch.argmax does."""
+    scripts/graph_decode_bench.py:55-112).  The logits are computed in
+    float64 and rounded to fp16 as the reference's fp16 F.linear returns
+    them; the argmax keeps the first index among equal fp16 values (as
+    torch.argmax does) and takes a NaN as the maximum.  Returns (token index
+    per batch row, float64 logits [B, V])."""
     logits = np.asarray(x, dtype=np.float64) @ np.asarray(w, dtype=np.float64).T
-    return np.argmax(logits, axis=-1), logits
+    l16 = logits.astype(np.float16).astype(np.float64)
+    nan = np.isnan(l16)
+    l16 = np.where(nan, np.inf, l16)
+    tok = np.where(nan.any(axis=-1), np.argmax(nan, axis=-1), np.argmax(l16, axis=-1))
+    return tok, logits

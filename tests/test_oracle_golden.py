@@ -176,3 +176,24 @@ def test_oracle_lm_head_argmax_first_index_on_ties():
     x = np.ones((2, 8), dtype=np.float16)
     tok, logits = O.lm_head_argmax(x, w)
     assert tok.tolist() == [1, 1] and logits.shape == (2, 5) and logits[0, 3] == 8.0
+
+
+@pytest.mark.parametrize("name", LAYERS)
+def test_torch_cpu_restatement_matches_reference(name):
+    """The timed CPU baseline (oracle/torch_cpu.py): bit-exact dequant and the
+    reference's tiled / cached outputs."""
+    import torch
+
+    from oracle import torch_cpu as T
+
+    g = load_golden("layers")
+    p = payload_from(g, f"{name}_")
+    w = T.decode_rows(p, 0, int(p["n"])).numpy()
+    assert hashlib.sha256(w.tobytes()).digest() == g[f"{name}_w_sha256"].tobytes()
+    x = torch.from_numpy(g[f"{name}_x"])
+    y = T.tiled_forward(p, x, T.rot_scale(p), tile_rows=256).numpy()
+    assert rel_l2(y, g[f"{name}_y_tiled"]) < 1e-5
+    yc = T.cached_forward(T.cached_weight(p), x).numpy()
+    if p["bias"] is not None:
+        yc = yc + p["bias"].astype(np.float32)
+    assert rel_l2(yc, g[f"{name}_y_cached"]) < 1e-3

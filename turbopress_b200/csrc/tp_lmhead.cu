@@ -40,9 +40,20 @@ __device__ __forceinline__ uint4 ld_stream16(const uint16_t* p) {
   return v;
 }
 
+// The reference's logits are fp16 (F.linear in fp16, then argmax): the key
+// ranks the fp16-rounded logit, so values that round together tie and the
+// first index wins.  Like torch.argmax, a NaN ranks above everything and -0
+// equals +0.
 __device__ __forceinline__ unsigned long long argmax_key(float v, unsigned idx) {
-  unsigned u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  float r = __half2float(__float2half_rn(v));
+  unsigned u;
+  if (r != r) {
+    u = 0xFFFFFFFFu;
+  } else {
+    if (r == 0.f) r = 0.f;
+    u = __float_as_uint(r);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
   return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - idx);
 }
 

@@ -120,12 +120,13 @@ struct alignas(16) StepHeader {
   int max_rt, attn_groups, pad[2];
 };
 
-constexpr int kMiscRecord = 0;     // stage record copy (sizeof(StepStage) <= 1024)
-constexpr int kMiscCodebook = 1024;
-constexpr int kMiscRed = 1152;     // [B + 1][16] fp32 reduction scratch (576 B)
-constexpr int kMiscFlags = 1792;   // barrier / last-CTA flags
-constexpr int kMiscBytes = 2048;
-static_assert(sizeof(StepStage) <= 1024, "stage record");
+constexpr int kRecordBytes = (sizeof(StepStage) + 15) / 16 * 16;
+constexpr int kMiscRecord = 0;                      // three stage-record slots
+constexpr int kMiscCodebook = 3 * kRecordBytes;     // 32 codebook words
+constexpr int kMiscRed = kMiscCodebook + 128;       // [B + 1][16] fp32 reduction scratch (576 B)
+constexpr int kMiscFlags = kMiscRed + 640;          // barrier / last-CTA flags
+constexpr int kMiscBytes = (kMiscFlags + 64 + 127) / 128 * 128;
+static_assert(kMiscBytes <= 2304, "stage records");
 
 #ifdef TP_STEP_TRACE
 // Development-only stage timeline (built only with -DTP_STEP_TRACE, never in
@@ -897,6 +898,27 @@ __device__ void attn_stage(const AttnStage& A, int B, int pos, unsigned char* sm
   }
 }
 
+// L2 bulk prefetch of the cached keys / values this CTA's attention items
+// will read (issued a stage ahead: the cache is far larger than L2).
+__device__ void prefetch_attention(const AttnStage& A, int B, int pos) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const int items = B * A.kv_heads * A.nsplit;
+  const int T = pos + 1, Ls = (T + A.nsplit - 1) / A.nsplit;
+  int n = 0;
+  for (int it = blockIdx.x; it < items; it += gridDim.x, ++n) {
+    if (lane != (2 * n) % 32 && lane != (2 * n + 1) % 32) continue;
+    const int grp = it / A.nsplit, sp = it - grp * A.nsplit;
+    const int t0 = sp * Ls, t1 = min(pos, t0 + Ls);  // the new token is not cached yet
+    if (t1 <= t0) continue;
+    const int64_t row = (int64_t)grp * A.max_t + t0;
+    const uint16_t* src = (lane & 1) ? A.v_cache : A.k_cache;
+    const unsigned bytes = (unsigned)(t1 - t0) * A.hd * 2u;
+    for (unsigned off = 0; off < bytes; off += 65536u)
+      prefetch_l2(src + row * A.hd + off / 2, min(65536u, bytes - off));
+  }
+}
+
 __device__ void final_norm_stage(const NormStage& N, int B, float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
@@ -933,7 +955,15 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     return;
   }
   const int pos = *pos_p;
-  StepStage& st = *reinterpret_cast<StepStage*>(smem + H.misc_off + kMiscRecord);
+  // stage records: slot s % 3 is in use, the next one has landed, the one
+  // after that is in flight (cp.async), so no stage reads its record from HBM
+  StepStage* slots = reinterpret_cast<StepStage*>(smem + H.misc_off + kMiscRecord);
+  auto fetch = [&](int idx) {
+    if (idx >= H.nstages) return;
+    for (int i = tid; i < (int)(sizeof(StepStage) / 16); i += kStepThreads)
+      cp_async16(reinterpret_cast<uint4*>(&slots[idx % 3]) + i, reinterpret_cast<const uint4*>(&stages[idx]) + i,
+                 true);
+  };
   uint32_t* cbs = reinterpret_cast<uint32_t*>(smem + H.misc_off + kMiscCodebook);
   // pair tables: bits <= 3 at shared-window address kLutAbs, 4-bit at the
   // start of the dynamic area (it spans the other one)
@@ -943,12 +973,16 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   float* red = reinterpret_cast<float*>(smem + H.misc_off + kMiscRed);
   const uint16_t* cur_cb = nullptr;
   int cur_bits = 0;
-  if (H.nstages > 0 && stages[0].type == kLinear) stage_rs_prefetch(stages[0].lin, smem);
+  fetch(0);
+  fetch(1);
+  cp_async_wait_all();
+  __syncthreads();
+  if (H.nstages > 0 && slots[0].type == kLinear) stage_rs_prefetch(slots[0].lin, smem);
   for (int s = 0; s < H.nstages; ++s) {
-    for (int i = tid; i < (int)(sizeof(StepStage) / 16); i += kStepThreads)
-      reinterpret_cast<uint4*>(&st)[i] = reinterpret_cast<const uint4*>(&stages[s])[i];
-    __syncthreads();
+    const StepStage& st = slots[s % 3];
+    fetch(s + 2);
     step_trace(s, 0);
+    if (s + 1 < H.nstages && slots[(s + 1) % 3].type == kAttention) prefetch_attention(slots[(s + 1) % 3].attn, H.B, pos);
     if (st.type == kLinear) {
       const LinearStage& L = st.lin;
       if (L.codebook != cur_cb || L.bits != cur_bits) {
@@ -973,10 +1007,12 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     }
     step_trace(s, 2);
     if (s + 1 == H.nstages) break;
-    if (stages[s + 1].type == kLinear) {
-      __syncthreads();  // this stage's shared buffers are free
-      prefetch_stage(stages[s + 1].lin);
-      stage_rs_prefetch(stages[s + 1].lin, smem);
+    cp_async_wait_all();  // the next records have landed
+    __syncthreads();      // and this stage's shared buffers are free
+    const StepStage& nx = slots[(s + 1) % 3];
+    if (nx.type == kLinear) {
+      prefetch_stage(nx.lin);
+      stage_rs_prefetch(nx.lin, smem);
     }
     if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x, s_ok)) break;
     step_trace(s, 3);

@@ -110,15 +110,37 @@ class DecodeEngine:
                                m.rot_scale.data_ptr(), x.data_ptr(), self.outputs[i].data_ptr(),
                                m.out_features, m.in_features, m.block,
                                _abi.dtype_code(x.dtype), -1 if dep is None else dep, 0)
-        nbytes = lib.tp_engine_image_bytes(n_ops)
-        self._image_host = np.zeros((nbytes + 15) // 16 * 16, dtype=np.uint8)  # numpy data is 16-aligned
-        with torch.cuda.device(dev):
-            _abi.check(lib.tp_engine_build(ops, n_ops, batch, first.bits, first.n_states,
-                                           self.codebook.data_ptr(), self._image_host.ctypes.data, nbytes),
-                       "engine_build")
-        self.image = torch.from_numpy(self._image_host).to(dev)
-        self.counters = torch.zeros(lib.tp_engine_counter_bytes(n_ops) // 4, dtype=torch.int32, device=dev)
+        self._ops = ops
         self.n_ops = n_ops
+        self._build(absolute_table=True)
+        self.counters = torch.zeros(lib.tp_engine_counter_bytes(n_ops) // 4, dtype=torch.int32, device=dev)
+        self._layout_checked = False
+
+    def _build(self, absolute_table: bool) -> None:
+        """Program image for this device.  With `absolute_table` the builder
+        may place the bits <= 3 pair table at a fixed shared-window address
+        (one permute per lookup); the kernel checks that layout before use."""
+        import os
+
+        lib = _abi.lib()
+        first = self.layers[0]
+        nbytes = lib.tp_engine_image_bytes(self.n_ops)
+        self._image_host = np.zeros((nbytes + 15) // 16 * 16, dtype=np.uint8)  # numpy data is 16-aligned
+        prev = os.environ.get("TP_ENGINE_NO_ABS")
+        if not absolute_table:
+            os.environ["TP_ENGINE_NO_ABS"] = "1"
+        try:
+            with torch.cuda.device(self.device):
+                _abi.check(lib.tp_engine_build(self._ops, self.n_ops, self.batch, first.bits, first.n_states,
+                                               self.codebook.data_ptr(), self._image_host.ctypes.data, nbytes),
+                           "engine_build")
+        finally:
+            if not absolute_table:
+                if prev is None:
+                    os.environ.pop("TP_ENGINE_NO_ABS", None)
+                else:
+                    os.environ["TP_ENGINE_NO_ABS"] = prev
+        self.image = torch.from_numpy(self._image_host).to(self.device)
 
     def set_input(self, x: Tensor) -> None:
         """Copy ``x`` [batch, d] into the external input of width d."""
@@ -136,6 +158,16 @@ class DecodeEngine:
             self.y_arena.zero_()
             self.counters.zero_()
             self.launch()
+            if not self._layout_checked and not torch.cuda.is_current_stream_capturing():
+                # first run: if the kernel found the shared-memory layout of
+                # the fixed-address pair table different from the planned
+                # one (status 3), rebuild with the relative layout and rerun
+                self._layout_checked = True
+                if int(self.counters[self.n_ops].item()) == 3:
+                    self._build(absolute_table=False)
+                    self.y_arena.zero_()
+                    self.counters.zero_()
+                    self.launch()
         return self.outputs
 
     def launch(self) -> None:
@@ -148,5 +180,8 @@ class DecodeEngine:
         """Raise if the last run gave up (a dependency or copy wait timed out)."""
         flag = int(self.counters[self.n_ops].item())
         if flag:
+            if flag == 3:
+                raise RuntimeError("decode engine aborted: the shared-memory layout differs from the one the "
+                                   "program was built for (fixed-address pair table); rebuild it")
             what = {1: "a dependency wait", 2: "a weight copy wait"}.get(flag, f"status {flag}")
             raise RuntimeError(f"decode engine aborted: {what} timed out")

@@ -239,6 +239,9 @@ class TPDecodeEngine:
 
     def check(self) -> None:
         flag = int(_view(self.counters_ptr + 4 * self.n_ops, (1,), self.device, "<u4").item())
+        if flag == 3:
+            raise RuntimeError(f"tensor-parallel engine aborted on rank {self.rank}: the shared-memory layout "
+                               "differs from the one the program was built for (set TP_ENGINE_NO_ABS=1 and rebuild)")
         if flag:
             what = {1: "a dependency wait", 2: "a weight copy wait"}.get(flag, f"status {flag}")
             raise RuntimeError(f"tensor-parallel engine aborted on rank {self.rank}: {what} timed out")
