@@ -68,6 +68,11 @@ LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down
 # DRAM bytes (read + write) of one engine launch / algorithmic bytes of the
 # step, from the ncu capture summarised under profiles/ (None: not captured)
 TRAFFIC_RATIO = 1.025
+# DRAM bytes (read 173.26 MB + write 9.01 MB) of one step_kernel launch over
+# the first 4 layers of the Qwen3-4B 3-bit batch-1 line / its algorithmic
+# bytes (169.12 MB); the traffic of every layer is the same, so the ratio
+# scales to the full step (profiles/step_kernel_qwen3-4b_4layer_3bit_b1.md)
+STEP_TRAFFIC = {("qwen3-4b", 3, 1): (173_256_960 + 9_010_176) / 169_115_520}
 
 
 def linear_shapes(cfg: dict) -> list[tuple[str, int, int]]:
@@ -520,6 +525,8 @@ def run_decode(args) -> dict | None:
         torch.cuda.synchronize()
 
     cfg = dict(SMODELS[args.model])
+    if args.layers > 0:  # profiling: the first layers of the model only
+        cfg["layers"] = args.layers
     B, bits = args.batch, args.bits
     tp_line = None
     if world > 1:
@@ -594,7 +601,9 @@ def run_decode(args) -> dict | None:
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(2 * steps),
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(ach / peak, 4), "traffic": None,
+                     "frac": round(ach / peak, 4),
+                     "traffic": (round(kbytes * STEP_TRAFFIC[(args.model, bits, B)])
+                                 if (args.model, bits, B) in STEP_TRAFFIC else None),
                      "kernel": "step_kernel (tp_step_run): step-kernel algorithmic bytes / CUDA-event duration, "
                                "mean over the timed launches",
                      "kernel_ms": round(ms_kernel, 4), "peak_source": peak_src},
@@ -873,7 +882,7 @@ def main() -> None:
     ap.add_argument("--parallel", choices=["replicas", "tp"], default="replicas",
                     help="N > 1: the line from N independent decode streams (replicas, with the tensor-parallel "
                          "engine of the decoder linears under 'tp') or the tensor-parallel engine itself")
-    ap.add_argument("--layers", type=int, default=0, help="tensor-parallel engine: decoder layers (profiling)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling: decoder layers of the model (0: all)")
     ap.add_argument("--workload", choices=["decode", "gemv", "lmhead"], default="decode",
                     help="decode: the contract line; gemv: the config-3 GEMV table; lmhead: the greedy LM head")
     ap.add_argument("--shapes", default="14336x4096", help="gemv --once: comma-separated NxD (out x in) shapes")

@@ -191,6 +191,19 @@ TP_API tp_status tp_tcq_gemv_noalloc(const void* x, int x_dtype, const uint16_t*
                                      int y_dtype, int64_t B, int64_t n, int64_t d, int64_t block,
                                      int bits, int n_states, void* stream);
 
+/* Reads (synchronizing `stream`) the status word that tp_tcq_gemv kernels
+ * leave in `workspace`: TP_OK, or TP_ERR_DEVICE when a kernel gave up (a
+ * bounded wait ran out: the outputs of that call are NaN; or the
+ * shared-memory layout check failed: they were not written).  Every
+ * completed call leaves the workspace's counter block zero; a call that gave
+ * up may not, so on TP_ERR_DEVICE the whole counter block (split-K counters
+ * and status) is cleared and the workspace is fit for the next call.  The
+ * reference has no device-side failure to report (its Triton kernel has no
+ * waits).  tp_gemv_noalloc_status does the same for the built-in scratch of
+ * tp_tcq_gemv_noalloc on the current device. */
+TP_API tp_status tp_gemv_status(const void* workspace, void* stream);
+TP_API tp_status tp_gemv_noalloc_status(void* stream);
+
 /* Skinny GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulator)
  * for batches of 16 and more: same arguments and result as tp_tcq_gemv.
  * The weights are decoded into shared memory (fp16, UMMA operand layout) and
@@ -361,7 +374,7 @@ TP_API tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* laye
 
 /* One decode step at position *pos_dev (device int: the number of tokens
  * already in the caches; the step writes k/v at that position).  Enqueued on
- * `stream` (graph-capturable: a 4-byte memset and one cooperative launch). */
+ * `stream` (graph-capturable: a 2 KB memset of the barrier block and one cooperative launch). */
 TP_API tp_status tp_step_run(const void* image_dev, const void* image_host, const int* pos_dev,
                              void* workspace, int64_t workspace_bytes, void* stream);
 
@@ -369,6 +382,16 @@ TP_API tp_status tp_step_run(const void* image_dev, const void* image_host, cons
  * step workspace: TP_OK, or TP_ERR_DEVICE when a grid barrier timed out or
  * the shared-memory layout check failed. */
 TP_API tp_status tp_step_status(const void* workspace, void* stream);
+
+/* Sets the grid-barrier limit of a built program (`image_host`, in
+ * microseconds; 0 = the default of 2 s) and the number of arrivals each
+ * barrier waits for beyond the grid's own (0 for every real run).  With
+ * extra_arrivals > 0 no barrier can complete: every CTA gives up after the
+ * limit, the step returns with incomplete outputs, and tp_step_status
+ * reports TP_ERR_DEVICE; the CUDA context stays usable.  This is how the
+ * timeout path is tested.  Copy the host image to the device again after
+ * the call. */
+TP_API tp_status tp_step_set_wait(void* image_host, int64_t barrier_us, int extra_arrivals);
 
 /* Reference-order GEMV straight from the format-v2 streams, any bits in 1..7:
  * y[B, n] = z[B, d] @ decode_rows^T (+ bias), z fp32 rotated activations.

@@ -22,7 +22,9 @@ import numpy as np
 import torch
 from torch import nn
 
-REF = os.environ.get("TURBOPRESS_REF", "/root/reference")
+REF = os.environ.get("TURBOPRESS_REF")
+if not REF:
+    sys.exit("set TURBOPRESS_REF to the reference TurboPress source tree (the folder holding turbopress/)")
 sys.path.insert(0, REF)
 
 from turbopress import pipeline as P  # noqa: E402

@@ -44,6 +44,8 @@ SIGNATURES: dict[str, tuple] = {
     "tp_gemv_workspace_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "tp_tcq_gemv": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _I64, _P]),
     "tp_tcq_gemv_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P]),
+    "tp_gemv_status": (_I, [_P, _P]),
+    "tp_gemv_noalloc_status": (_I, [_P]),
     "tp_gemm_tc_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "tp_tcq_gemm_tc": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _I64, _P]),
     "tp_lm_head_workspace_bytes": (_I64, [_I64]),
@@ -64,6 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "tp_step_build": (_I, [_P, _P, _P, _I64, _P]),
     "tp_step_run": (_I, [_P, _P, _P, _P, _I64, _P]),
     "tp_step_status": (_I, [_P, _P]),
+    "tp_step_set_wait": (_I, [_P, _I64, _I]),
 }
 
 

@@ -790,6 +790,31 @@ extern "C" tp_status tp_tcq_gemv(const void* x, int x_dtype, const uint16_t* rot
   return clear_ok();
 }
 
+// Status word of a GEMV workspace.  A call that completes leaves the
+// counter block zero; one whose kernel gave up (a bounded wait ran out, or
+// the shared-memory layout check failed) sets a status bit and may leave
+// split-K counters part-way, which would make the next call on the same
+// workspace combine the wrong partial sums.  So a nonzero status clears the
+// whole counter block (counters and status) before it is reported.
+namespace tp {
+tp_status gemv_status_at(const unsigned char* ws, cudaStream_t st, const char* who) {
+  unsigned v = 0;
+  TP_CUDA_TRY(cudaMemcpyAsync(&v, ws + kStatusOff, 4, cudaMemcpyDeviceToHost, st), "status copy");
+  TP_CUDA_TRY(cudaStreamSynchronize(st), "status sync");
+  if (v == 0) return clear_ok();
+  TP_CUDA_TRY(cudaMemsetAsync(const_cast<unsigned char*>(ws), 0, kCounterBytes, st), "counter block clear");
+  TP_CUDA_TRY(cudaStreamSynchronize(st), "counter block clear sync");
+  if (v & kStatusLayout)
+    return fail(TP_ERR_DEVICE, "%s: shared-memory layout check failed, outputs not written (status %u)", who, v);
+  return fail(TP_ERR_DEVICE, "%s: a bounded device wait ran out, outputs are NaN (status %u)", who, v);
+}
+}  // namespace tp
+
+extern "C" tp_status tp_gemv_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(TP_ERR_ARG, "tp_gemv_status: null workspace");
+  return gemv_status_at(static_cast<const unsigned char*>(workspace), as_stream(stream), "tp_tcq_gemv");
+}
+
 extern "C" tp_status tp_gemv_v2(const float* z, const uint8_t* path_packed, const uint8_t* member_packed,
                                 const uint16_t* scales, const uint16_t* codebook, const uint16_t* bias, void* y,
                                 int y_dtype, int64_t B, int64_t n, int64_t d, int bits, int n_states, void* stream) {

@@ -21,6 +21,10 @@ inline int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
 int sm_count();
 
+// Reads the status word of the workspace at `ws` (synchronizing `st`); a
+// nonzero status clears the counter block and is reported as TP_ERR_DEVICE.
+tp_status gemv_status_at(const unsigned char* ws, cudaStream_t st, const char* who);
+
 // One fused rotate + decode + GEMV problem (batch <= kSkMaxBatch).
 struct SkRequest {
   const void* x;

@@ -63,3 +63,10 @@ extern "C" tp_status tp_tcq_gemv_noalloc(const void* x, int x_dtype, const uint1
   return tp_tcq_gemv(x, x_dtype, rot_scale, tcq_stream, scales, codebook, bias, y, y_dtype, B, n, d, block, bits,
                      n_states, scratch, kNoAllocScratchBytes, stream);
 }
+
+extern "C" tp_status tp_gemv_noalloc_status(void* stream) {
+  void* scratch = nullptr;
+  cudaStream_t st = as_stream(stream);
+  if (tp_status s = scratch_for_current_device(&scratch, st)) return s;
+  return gemv_status_at(static_cast<const unsigned char*>(scratch), st, "tp_tcq_gemv_noalloc");
+}

@@ -117,7 +117,12 @@ struct alignas(16) StepHeader {
   int nstages, B, grid, has4;
   uint32_t base, dyn, lut_off, misc_off;
   int64_t ws_part_off, ws_attn_off, ws_bytes;
-  int max_rt, attn_groups, pad[2];
+  int max_rt, attn_groups;
+  // grid-barrier limit in microseconds (0: kBarrierNs), and arrivals a
+  // barrier waits for beyond the grid's own (0 in every program that runs a
+  // model; tp_step_set_wait raises it to make the waits run out on purpose)
+  unsigned barrier_us;
+  int extra_arrivals;
 };
 
 constexpr int kRecordBytes = (sizeof(StepStage) + 15) / 16 * 16;
@@ -163,7 +168,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // (after a release fence) and spins on acquire loads until `target`; bounded
 // by kBarrierNs of global time, after which it sets the status and every
 // CTA abandons the step.
-__device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, int* s_ok) {
+__device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, unsigned long long limit_ns,
+                             int* s_ok) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -175,7 +181,7 @@ __device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, i
         ok = 1;
         break;
       }
-      if ((i & 255u) == 255u && (global_ns() - t0 > kBarrierNs || (ld_acquire(status) & kStepStatusBarrier))) break;
+      if ((i & 255u) == 255u && (global_ns() - t0 > limit_ns || (ld_acquire(status) & kStepStatusBarrier))) break;
     }
     if (!ok) atomicOr(status, kStepStatusBarrier);
     *s_ok = ok;
@@ -955,6 +961,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     return;
   }
   const int pos = *pos_p;
+  const unsigned long long limit_ns = H.barrier_us ? 1000ull * H.barrier_us : kBarrierNs;
   // stage records: slot s % 3 is in use, the next one has landed, the one
   // after that is in flight (cp.async), so no stage reads its record from HBM
   StepStage* slots = reinterpret_cast<StepStage*>(smem + H.misc_off + kMiscRecord);
@@ -1014,7 +1021,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
       prefetch_stage(nx.lin);
       stage_rs_prefetch(nx.lin, smem);
     }
-    if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x, s_ok)) break;
+    if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x + (unsigned)H.extra_arrivals, limit_ns, s_ok)) break;
     step_trace(s, 3);
   }
 }
@@ -1382,6 +1389,8 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   H->ws_attn_off = H->ws_part_off + align256(part_floats * 4);
   H->ws_bytes = H->ws_attn_off + align256((int64_t)attn_groups * nsplit * gs * (hd + 2) * 4);
   H->max_rt = static_cast<int>(rt_max);
+  H->barrier_us = 0;
+  H->extra_arrivals = 0;
   H->attn_groups = attn_groups;
   *workspace_bytes = H->ws_bytes;
   return clear_ok();
@@ -1424,6 +1433,15 @@ extern "C" tp_status tp_step_run(const void* image_dev, const void* image_host, 
                                           st),
               "step_kernel launch");
   return check_launch("step_kernel");
+}
+
+extern "C" tp_status tp_step_set_wait(void* image_host, int64_t barrier_us, int extra_arrivals) {
+  if (!image_host || barrier_us < 0 || barrier_us > 60000000 || extra_arrivals < 0)
+    return fail(TP_ERR_ARG, "tp_step_set_wait: bad argument");
+  StepHeader* H = static_cast<StepHeader*>(image_host);
+  H->barrier_us = static_cast<unsigned>(barrier_us);
+  H->extra_arrivals = extra_arrivals;
+  return clear_ok();
 }
 
 extern "C" tp_status tp_step_status(const void* workspace, void* stream) {

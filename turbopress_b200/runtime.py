@@ -185,8 +185,28 @@ class _WorkspacePool:
                 self._bufs[idx] = buf
             return buf
 
+    def check(self, device: torch.device | None = None) -> None:
+        """Raise if a GEMV kernel on `device` gave up since the last check
+        (tp_gemv_status; it also clears the counter block so the workspace
+        is fit for the next call).  Synchronizes the current stream."""
+        idx = (device.index if device is not None and device.index is not None
+               else torch.cuda.current_device())
+        buf = self._bufs.get(idx)
+        if buf is None:
+            return
+        with torch.cuda.device(idx):
+            st = _abi.lib().tp_gemv_status(buf.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _abi.check(st, "tcq_gemv (device status)")
+
 
 WORKSPACE = _WorkspacePool()
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Raise RuntimeError when a packed GEMV on `device` reported a device-side
+    failure (a bounded wait that ran out, or a failed layout check) since the
+    last check; the affected outputs are NaN or unwritten."""
+    WORKSPACE.check(device)
 # the tcgen05 path scribbles over its workspace: it must not share the GEMV's
 # (whose split-K counter block has to stay zero between calls)
 WORKSPACE_TC = _WorkspacePool()

@@ -178,6 +178,17 @@ class DecodeStep:
         st = torch.cuda.current_stream(self.device).cuda_stream
         _abi.check(_abi.lib().tp_step_status(self.workspace.data_ptr(), st), "step")
 
+    def set_wait(self, barrier_us: int = 0, extra_arrivals: int = 0) -> None:
+        """Grid-barrier limit (microseconds; 0 restores the 2 s default) and
+        extra arrivals each barrier waits for.  ``extra_arrivals > 0`` is a
+        wait that nothing satisfies: the step gives up after ``barrier_us``,
+        leaves its outputs incomplete and ``status()`` raises.  Used to test
+        the timeout path; every model run keeps 0."""
+        _abi.check(_abi.lib().tp_step_set_wait(ctypes.addressof(self._image_host), int(barrier_us),
+                                               int(extra_arrivals)), "step_set_wait")
+        host = torch.frombuffer(bytearray(self._image_host), dtype=torch.uint8)
+        self.image.copy_(host)
+
     def advance(self) -> None:
         """pos += 1 on the device (graph-capturable)."""
         self.pos.add_(1)
