@@ -136,16 +136,22 @@ static_assert(kMiscBytes <= 2304, "stage records");
 #ifdef TP_STEP_TRACE
 // Development-only stage timeline (built only with -DTP_STEP_TRACE, never in
 // the shipped library): %globaltimer per stage, CTA and phase.
-__device__ unsigned long long g_step_trace[256][160][4];
+__device__ unsigned long long g_step_trace[256][160][8];
+__shared__ int s_step_trace_stage;
 __device__ __forceinline__ void step_trace(int s, int k) {
   if (threadIdx.x == 0 && blockIdx.x < 160 && s < 256) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_step_trace[s][blockIdx.x][k] = t;
+    // SM cycle counter: differences are meaningful within one CTA
+    g_step_trace[s][blockIdx.x][k] = static_cast<unsigned long long>(clock64());
+    if (k == 0) s_step_trace_stage = s;
   }
+}
+// a mark inside a stage (thread 0 of the CTA)
+__device__ __forceinline__ void step_mark(int k) {
+  if (threadIdx.x == 0 && blockIdx.x < 160) step_trace(s_step_trace_stage, k);
 }
 #else
 __device__ __forceinline__ void step_trace(int, int) {}
+__device__ __forceinline__ void step_mark(int) {}
 #endif
 
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
@@ -450,7 +456,7 @@ __device__ void stage_rs_prefetch(const LinearStage& L, unsigned char* smem) {
 // Stage prologue: rotation scales to shared memory (async), the input
 // transform, every op's rotated activations, and the zero rows (CTAs of a
 // K-slice: the slice's columns).
-__device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
+__device__ __forceinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
   const int tid = threadIdx.x;
   const int slice = blockIdx.x / L.cps;
   if (slice >= L.kparts) return;
@@ -464,6 +470,7 @@ __device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char*
   for (int b0 = 0; b0 < B; b0 += L.rpp) {
     const int rows = min(L.rpp, B - b0);
     stage_input(L, b0, rows, c0, cols, xin, red);
+    step_mark(4);
     if (L.lg_block <= 9 && L.rs_smem) {
       if (L.lg_block == 9) rotate_small_blocks<16>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
       else rotate_small_blocks<8>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
@@ -473,6 +480,7 @@ __device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char*
                      z + (k * (B + 1) + b0) * zst, zst);
     }
   }
+  step_mark(5);
   for (int i = tid; i < L.nops * (cols / 8); i += kStepThreads) {
     const int k = i / (cols / 8), r = i - k * (cols / 8);
     reinterpret_cast<uint4*>(z + (k * (B + 1) + B) * zst)[r] = make_uint4(0u, 0u, 0u, 0u);
@@ -550,6 +558,7 @@ __device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char
 #pragma unroll
     for (int q = 0; q < 2; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
     const bool solo = L.kparts == 1 && j0 <= frt * Us && (frt + 1) * Us <= j1;
+    step_mark(6);
     if (!solo) {
       const int rank = wl - sp.warp_of(frt * Us);
       float* pc = part + ((int64_t)(frt * L.kparts + slice) * L.maxc + rank) * 16 * B;
@@ -569,6 +578,7 @@ __device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char
         last = atomicAdd(&counters[frt], 1u) == (unsigned)((L.kparts - 1) * c0_ + c1_ - 1) ? 1u : 0u;
       last = __shfl_sync(0xffffffffu, last, 0);
       if (!last) return;
+      step_mark(7);
       __threadfence();
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = 0.f;
@@ -772,6 +782,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
     }
   }
   __syncthreads();
+  step_mark(4);
   // per-warp online softmax over its tokens
   float qv[G][E], m[G], l[G], acc[G][E];
 #pragma unroll
@@ -815,6 +826,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
 #pragma unroll
     for (int e = 0; e < E; ++e) kx[e] = kn[e], vx[e] = vn[e];
   }
+  step_mark(5);
   // combine the warps
   const int ws_ = hd + 2;
 #pragma unroll
@@ -849,6 +861,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   __syncthreads();
   if (tid == 0) *s_last = atomicAdd(&counters[cgroup], 1u) == (unsigned)(A.nsplit - 1) ? 1u : 0u;
   __syncthreads();
+  step_mark(6);
   if (!*s_last) return;
   __threadfence();
   const float* gp = part + (int64_t)cgroup * A.nsplit * gs * ws_;
@@ -859,6 +872,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
     ml[2 * i + 1] = __ldcg(gp + i * ws_ + 1);
   }
   __syncthreads();
+  step_mark(1);
   for (int i = tid; i < gs * hd; i += kStepThreads) {
     const int j = i / hd, dd = i - j * hd;
     float M = -INFINITY;
@@ -879,6 +893,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
     }
     A.out[(int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd] = f2h(Ad / Lsum);
   }
+  step_mark(7);
   if (tid == 0) counters[cgroup] = 0u;
 }
 
