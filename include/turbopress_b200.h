@@ -358,6 +358,12 @@ typedef struct tp_step_model {
   uint16_t* hidden_state;       /* fp16 [B][hidden]: input embeddings in, residual   */
   uint16_t* final_out;          /* fp16 [B][hidden]: final RMSNorm output            */
   void* act;                    /* tp_step_act_bytes() bytes of activation scratch   */
+  /* Optional RoPE tables, fp16 [max_tokens][head_dim/2]: cos / sin of the
+   * fp32 angle pos * inv_freq[i], rounded to fp16 (what the reference model's
+   * rotary embedding feeds its fp16 forward).  NULL: the kernel evaluates
+   * them from inv_freq (slower). */
+  const uint16_t* rope_cos;
+  const uint16_t* rope_sin;
 } tp_step_model;
 
 /* Bytes of the step program image for `layers` layers / of the activation
@@ -372,6 +378,13 @@ TP_API int64_t tp_step_act_bytes(const tp_step_model* m);
 TP_API tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* layers, void* image_host,
                                int64_t image_bytes, int64_t* workspace_bytes);
 
+/* Resolves the workspace buffers a built image refers to (fp32 projection
+ * accumulators, the second residual buffer) against `workspace` (256-byte
+ * aligned, *workspace_bytes from tp_step_build, zero-filled once).  Call once
+ * per image, before copying it to the device; tp_step_run refuses an image
+ * bound to another workspace. */
+TP_API tp_status tp_step_bind(void* image_host, void* workspace, int64_t workspace_bytes);
+
 /* One decode step at position *pos_dev (device int: the number of tokens
  * already in the caches; the step writes k/v at that position).  Enqueued on
  * `stream` (graph-capturable: a 2 KB memset of the barrier block and one cooperative launch). */
@@ -380,7 +393,9 @@ TP_API tp_status tp_step_run(const void* image_dev, const void* image_host, cons
 
 /* Reads (synchronizing `stream`) and clears the device status word of a
  * step workspace: TP_OK, or TP_ERR_DEVICE when a grid barrier timed out or
- * the shared-memory layout check failed. */
+ * the shared-memory layout check failed.  After a failed step it also clears
+ * the accumulators and attention counters the step left part-written, so the
+ * next step starts clean (its outputs are not valid). */
 TP_API tp_status tp_step_status(const void* workspace, void* stream);
 
 /* Sets the grid-barrier limit of a built program (`image_host`, in

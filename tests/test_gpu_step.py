@@ -125,7 +125,10 @@ def test_step_graph_replay_advances_position():
     for i in range(3):
         graph.replay()
         torch.cuda.synchronize()
-        assert torch.equal(step.final_out, outs[i])
+        # the linears add their K-range partial sums with fp32 atomics, so the
+        # summation order (and the last fp16 ulp of a few outputs) varies
+        # between runs; nothing else may differ
+        assert _rel(step.final_out, outs[i]) < 2e-3, i
     assert int(step.pos.item()) == 13
 
 

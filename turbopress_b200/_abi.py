@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
     "tp_step_image_bytes": (_I64, [_I]),
     "tp_step_act_bytes": (_I64, [_P]),
     "tp_step_build": (_I, [_P, _P, _P, _I64, _P]),
+    "tp_step_bind": (_I, [_P, _P, _I64]),
     "tp_step_run": (_I, [_P, _P, _P, _P, _I64, _P]),
     "tp_step_status": (_I, [_P, _P]),
     "tp_step_set_wait": (_I, [_P, _I64, _I]),

@@ -48,48 +48,63 @@ constexpr unsigned long long kBarrierNs = 2000000000ull;  // a grid barrier give
 
 enum StageType : int { kLinear = 0, kAttention = 1, kFinalNorm = 2 };
 enum InKind : int { kInPlain = 0, kInRmsNorm = 1, kInSiluMul = 2 };
-enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1 };
 
 // workspace words
 constexpr int64_t kWsStatus = 64;      // status bits (kStepStatus*)
+constexpr int64_t kWsLayout = 128;     // [acc offset, acc bytes] (int64), written by every run
 constexpr int64_t kWsFlags = 1024;     // grid barrier counter (zeroed before each run)
 constexpr int kMaxGrid = 512;
-constexpr int64_t kWsCounters = kWsFlags + 4 * kMaxGrid;  // per-row-tile / per-attention-group counters
+constexpr int64_t kWsCounters = kWsFlags + 4 * kMaxGrid;  // per-attention-group counters
 constexpr unsigned kStepStatusLayout = 1u, kStepStatusBarrier = 2u;
+// pointer fields of a built image that name workspace buffers hold
+// kWsTag | offset until tp_step_bind resolves them
+constexpr uintptr_t kWsTag = uintptr_t(1) << 62;
 
+// A linear op writes raw fp32 dot products (before its row scale) into an
+// accumulator with red.add; the stages that read the op's output apply
+// scale / bias and the fp16 rounding of the reference there.
 struct alignas(16) StepOp {
   const unsigned char* stream;
-  const uint16_t* scales;
+  float* acc;  // fp32 [B][n], zero before the stage
   const uint16_t* rot_scale;
-  const uint16_t* bias;
-  uint16_t* out;  // fp16 [B][n]
   int n, row_tiles, rt_off, pad;
+};
+
+// An input vector of a stage: r16(base + r16(acc * scale + bias)) with the
+// terms that are present (base alone: a plain fp16 input).
+struct alignas(16) InVec {
+  const uint16_t* base;   // fp16 [B][d] or null
+  const float* acc;       // fp32 [B][d] or null
+  const uint16_t* scale;  // fp16 [d] (with acc)
+  const uint16_t* bias;   // fp16 [d] or null
 };
 
 struct alignas(16) LinearStage {
   const uint16_t* codebook;
-  const uint16_t* in0;    // [B][d] fp16: x (plain / norm) or gate (SiLU product)
-  const uint16_t* in1;    // [B][d] fp16: up (SiLU product)
   const uint16_t* gamma;  // [d] fp16 norm weight
-  int nops, in_kind, epi, bits;
-  int d, d_pad, units_k, lg_block;
+  uint16_t* hout;         // norm input: the reconstructed residual is written here
+  InVec in[2];            // plain / norm: in[0]; SiLU product: gate in[0], up in[1]
+  int nops, in_kind, bits, d;
+  int d_pad, units_k, lg_block, kparts;
   float norm, eps;
-  int kparts, us, cps, maxc, rt_total, rpp, rs_smem, pad2[3];
-  uint32_t z_off, xin_off, scr_off, rs_off;  // shared-memory offsets from the dynamic base
+  int us, cps, rt_total, rpp, rs_smem, nin, pad2[2];
+  // shared-memory offsets from the dynamic base: activations, input rows,
+  // fp32 scratch, rotation scales, norm weight, producer scales
+  uint32_t z_off, xin_off, scr_off, rs_off, gam_off, psc_off, pad3[2];
   SliceSplit split[2];
   StepOp ops[kMaxStageOps];
 };
 
 struct alignas(16) AttnStage {
-  const uint16_t* q;  // [B][q_heads*hd] fp16 (q_proj output)
-  const uint16_t* k;  // [B][kv_heads*hd]
-  const uint16_t* v;
+  InVec q, k, v;  // q_proj / k_proj / v_proj outputs (accumulators + scales)
   const uint16_t* q_norm;  // [hd] or null
   const uint16_t* k_norm;
   uint16_t* k_cache;  // [B][kv_heads][max_t][hd]
   uint16_t* v_cache;
   uint16_t* out;  // [B][q_heads*hd]
   const float* inv_freq;  // [hd/2]
+  const uint16_t* rope_cos;  // [max_t][hd/2] fp16 or null (then computed)
+  const uint16_t* rope_sin;
   int q_heads, kv_heads, hd, max_t;
   int nsplit;
   float eps, scaling;
@@ -97,15 +112,21 @@ struct alignas(16) AttnStage {
 };
 
 struct alignas(16) NormStage {
-  const uint16_t* x;
+  InVec x;  // residual base + down_proj accumulator
   const uint16_t* gamma;
   uint16_t* out;
+  uint16_t* hout;  // the final residual stream
   int d;
   float eps;
+  uint32_t buf_off;  // fp16 [d] row buffer in shared memory
 };
 
 struct alignas(16) StepStage {
-  int type, pad[3];
+  int type, nzero, pad[2];
+  // buffers every CTA clears (grid-stride) at the start of the stage: the
+  // accumulators whose readers finished in an earlier stage
+  float* zero_ptr[2];
+  int64_t zero_bytes[2];
   union {
     LinearStage lin;
     AttnStage attn;
@@ -116,8 +137,9 @@ struct alignas(16) StepStage {
 struct alignas(16) StepHeader {
   int nstages, B, grid, has4;
   uint32_t base, dyn, lut_off, misc_off;
-  int64_t ws_part_off, ws_attn_off, ws_bytes;
-  int max_rt, attn_groups;
+  int64_t ws_acc_off, ws_acc_bytes, ws_attn_off, ws_h2_off, ws_bytes;
+  int attn_groups, pad0;
+  uint64_t bound_ws;  // the workspace tp_step_bind resolved the image's workspace pointers against
   // grid-barrier limit in microseconds (0: kBarrierNs), and arrivals a
   // barrier waits for beyond the grid's own (0 in every program that runs a
   // model; tp_step_set_wait raises it to make the waits run out on purpose)
@@ -131,7 +153,7 @@ constexpr int kMiscCodebook = 3 * kRecordBytes;     // 32 codebook words
 constexpr int kMiscRed = kMiscCodebook + 128;       // [B + 1][16] fp32 reduction scratch (576 B)
 constexpr int kMiscFlags = kMiscRed + 640;          // barrier / last-CTA flags
 constexpr int kMiscBytes = (kMiscFlags + 64 + 127) / 128 * 128;
-static_assert(kMiscBytes <= 2304, "stage records");
+static_assert(kMiscBytes <= 3072, "stage records");
 
 #ifdef TP_STEP_TRACE
 // Development-only stage timeline (built only with -DTP_STEP_TRACE, never in
@@ -204,100 +226,164 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-__device__ __forceinline__ float sumsq8(uint4 v) {
+__device__ __forceinline__ void unpack8(uint4 v, float* f) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float s = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-    s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
   }
-  return s;
+}
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __half2 h = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+    w[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Input transform of rows [b0, b0+rows) over slice columns [c0, c0+cols):
-// xin (fp16 bits, [rows][cols]) = the stage's input as the reference rounds
-// it.  Every thread issues all of its 16-byte loads of a round before using
-// them (one memory round trip per round of 512 chunks of 8 columns).
-__device__ __forceinline__ uint4 transform8(int kind, uint4 xv, uint4 uv, uint4 gv, float r) {
-  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-  uint32_t ow[4];
-  if (kind == kInRmsNorm) {
-    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+// Raw loads of one 8-column chunk of an input vector (row offset `ro`,
+// column c): the dynamic parts (base, accumulator) come from L2 (.cg: other
+// SMs wrote them during this launch); scales from shared memory (`ssc`,
+// staged before the stage's barrier) or global; bias from global.
+struct ChunkRaw {
+  uint4 base;
+  float4 a0, a1;
+};
+// BASE / ACC: which terms the vector has (fixed per call site, so the
+// registers of absent terms are not kept)
+template <bool BASE, bool ACC>
+__device__ __forceinline__ void load_chunk(const InVec& V, int64_t ro, int c, ChunkRaw& r) {
+  if constexpr (BASE) r.base = __ldcg(reinterpret_cast<const uint4*>(V.base + ro + c));
+  if constexpr (ACC) {
+    r.a0 = __ldcg(reinterpret_cast<const float4*>(V.acc + ro + c));
+    r.a1 = __ldcg(reinterpret_cast<const float4*>(V.acc + ro + c + 4));
+  }
+}
+// the vector's 8 values (fp16-exact floats): r16(base + r16(acc * scale + bias));
+// scales at ssc[cs..], bias at global column cg
+template <bool BASE, bool ACC>
+__device__ __forceinline__ void finish_chunk(const InVec& V, const ChunkRaw& r, const uint16_t* ssc, int cs, int cg,
+                                             float* f) {
+  float b[8];
+  if constexpr (BASE) unpack8(r.base, b);
+  if constexpr (ACC) {
+    float sc[8], bi[8];
+    unpack8(*reinterpret_cast<const uint4*>(ssc + cs), sc);
+    const bool hb = V.bias != nullptr;
+    if (hb) unpack8(*reinterpret_cast<const uint4*>(V.bias + cg), bi);
+    const float a[8] = {r.a0.x, r.a0.y, r.a0.z, r.a0.w, r.a1.x, r.a1.y, r.a1.z, r.a1.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
-      const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&gw[e]));
-      const __half2 hv = __floats2half2_rn(gf.x * r16(xf.x * r), gf.y * r16(xf.y * r));
-      ow[e] = *reinterpret_cast<const uint32_t*>(&hv);
-    }
-  } else if (kind == kInSiluMul) {
-    const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 gf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
-      const float2 uf = __half22float2(*reinterpret_cast<const __half2*>(&uw[e]));
-      const float a0 = r16(gf.x / (1.f + __expf(-gf.x))), a1 = r16(gf.y / (1.f + __expf(-gf.y)));
-      const __half2 hv = __floats2half2_rn(a0 * uf.x, a1 * uf.y);
-      ow[e] = *reinterpret_cast<const uint32_t*>(&hv);
+    for (int e = 0; e < 8; ++e) {
+      float o = a[e] * sc[e];
+      if (hb) o += bi[e];
+      f[e] = BASE ? r16(b[e] + r16(o)) : r16(o);
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ow[e] = xw[e];
+    for (int e = 0; e < 8; ++e) f[e] = b[e];
   }
-  return make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // Input transform of rows [b0, b0+rows) over slice columns [c0, c0+cols):
-// xin (fp16 bits, [rows][cols]) = the stage's input as the reference rounds
-// it.  Warps split over the rows (fixed order: deterministic sums); every
-// lane issues all its 16-byte loads of a round before using them, and when a
-// row fits one round the norm's sum of squares comes from the same loads.
-__device__ __forceinline__ void stage_input(const LinearStage& L, int b0, int rows, int c0, int cols,
-                                            uint16_t* xin, float* red) {
+// xin (fp16 bits, [rows][cols]) holds
+//   plain:    the input row;
+//   RMS norm: the residual h = r16(base + r16(acc*scale + bias)) (the norm
+//             itself, r16(gamma * r16(h * rinv)), is applied by the rotation
+//             with rinv[row] from here); h is also written back to L.hout,
+//             each CTA of the K-slice writing its share of the chunks;
+//   SiLU:     r16(r16(silu(gate)) * up).
+// Warps split over the rows (fixed order: deterministic sums); every lane
+// issues all its loads of a round before using them.
+template <int KIND, bool ACC>
+__device__ __forceinline__ void stage_input_k(const LinearStage& L, int b0, int rows, int c0, int cols, uint16_t* xin,
+                                              float* red, const unsigned char* smem) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* rinv = red + kStepMaxBatch * kStepWarps;
   const int wpr = kStepWarps / rows, row = warp / wpr, sub = warp - row * wpr;
   const bool act = row < rows;
   const int64_t xrow = (int64_t)(b0 + (act ? row : 0)) * L.d;
-  constexpr int U = 4;  // 16-byte loads per lane in flight
+  // chunks per lane in flight (registers: 4 / 12 / 16 per chunk)
+  constexpr int U = KIND == kInPlain ? 4 : KIND == kInRmsNorm ? 3 : 2;
   const int stride = wpr * 32;
   const int cpr = cols >> 3;
-  const bool norm = L.in_kind == kInRmsNorm;
-  // one round covers the whole row: load once, norm from the same registers
-  const bool single = cols == L.d && cpr <= stride * U;
-  uint4 xv[U], uv[U], gv[U];
-  auto load_round = [&](int cb) {
+  constexpr bool norm = KIND == kInRmsNorm, silu = KIND == kInSiluMul;
+  constexpr bool BASE = KIND != kInSiluMul;
+  const uint16_t* psc = reinterpret_cast<const uint16_t*>(smem + L.psc_off);
+  // CTAs of this K-slice share the write-back of h
+  const int slice = blockIdx.x / L.cps, cta_in = blockIdx.x - slice * L.cps;
+  float ssum = 0.f;
+  ChunkRaw r0[U], r1[silu ? U : 1];
+#define TP_STEP_ISSUE(CB)                                      \
+  _Pragma("unroll") for (int u = 0; u < U; ++u) {              \
+    const int ci = (CB) + u * stride, c = c0 + ci * 8;         \
+    if (ci < cpr && c < L.d) {                                 \
+      load_chunk<BASE, ACC>(L.in[0], xrow, c, r0[u]);          \
+      if constexpr (silu) load_chunk<false, true>(L.in[1], xrow, c, r1[u]); \
+    }                                                          \
+  }
+  const int cb0 = sub * 32 + lane;
+  if (act) {
+    TP_STEP_ISSUE(cb0)
+  }
+  // the stage's static vectors (cp.async group issued before its barrier;
+  // the newest group is a stage record still in flight)
+  cp_async_wait_group1();
+  __syncthreads();
+  for (int cb = cb0; act && cb < cpr; cb += stride * U) {
+    if (cb != cb0) {
+      TP_STEP_ISSUE(cb)
+    }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int ci = cb + u * stride, c = c0 + ci * 8;
-      if (act && ci < cpr && c < L.d) {
-        xv[u] = *reinterpret_cast<const uint4*>(L.in0 + xrow + c);
-        if (L.in_kind == kInSiluMul) uv[u] = *reinterpret_cast<const uint4*>(L.in1 + xrow + c);
-        if (norm) gv[u] = *reinterpret_cast<const uint4*>(L.gamma + c);
-      }
-    }
-  };
-  if (single) load_round(sub * 32 + lane);
-  if (norm) {
-    float ssum = 0.f;
-    if (single) {
+      if (ci >= cpr) break;
+      uint4 o = make_uint4(0u, 0u, 0u, 0u);
+      if (c < L.d) {
+        float f[8];
+        finish_chunk<BASE, ACC>(L.in[0], r0[u], psc, ci * 8, c, f);
+        if constexpr (silu) {
+          float up[8];
+          finish_chunk<false, true>(L.in[1], r1[u], psc + cols, ci * 8, c, up);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int ci = sub * 32 + lane + u * stride;
-        if (act && ci < cpr) ssum += sumsq8(xv[u]);
+          for (int e = 0; e < 8; ++e) f[e] = r16(r16(f[e] / (1.f + __expf(-f[e]))) * up[e]);
+        }
+        o = pack8(f);
+        if constexpr (norm) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
+          if (L.hout && ci % L.cps == cta_in) *reinterpret_cast<uint4*>(L.hout + xrow + c) = o;
+        }
       }
-    } else {
+      *reinterpret_cast<uint4*>(xin + row * cols + ci * 8) = o;
+    }
+  }
+#undef TP_STEP_ISSUE
+  if constexpr (norm) {
+    if (cols != L.d) {
+      // K-split: the sum of squares needs the whole row (scales from global)
+      ssum = 0.f;
       const int dpr = L.d >> 3;
       for (int cb = sub * 32 + lane; act && cb < dpr; cb += stride * U) {
-        uint4 v[U];
+        ChunkRaw r0[U];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (cb + u * stride < dpr) v[u] = *reinterpret_cast<const uint4*>(L.in0 + xrow + (cb + u * stride) * 8);
+          if (cb + u * stride < dpr) load_chunk<BASE, ACC>(L.in[0], xrow, (cb + u * stride) * 8, r0[u]);
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (cb + u * stride < dpr) ssum += sumsq8(v[u]);
+        for (int u = 0; u < U; ++u) {
+          const int c = (cb + u * stride) * 8;
+          if (c >= L.d) break;
+          float f[8];
+          finish_chunk<BASE, ACC>(L.in[0], r0[u], L.in[0].scale, c, c, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
+        }
       }
     }
     for (int o = 16; o; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
@@ -308,21 +394,31 @@ __device__ __forceinline__ void stage_input(const LinearStage& L, int b0, int ro
       for (int w = 0; w < wpr; ++w) sv += red[tid * wpr + w];
       rinv[tid] = rsqrtf(sv / (float)L.d + L.eps);
     }
-    __syncthreads();
   }
-  const float r = norm && act ? rinv[row] : 1.f;
-  for (int cb = sub * 32 + lane; act && cb < cpr; cb += stride * U) {
-    if (!single) load_round(cb);
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int ci = cb + u * stride, c = c0 + ci * 8;
-      if (ci >= cpr) break;
-      const uint4 o = c < L.d ? transform8(L.in_kind, xv[u], uv[u], gv[u], r) : make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(xin + row * cols + ci * 8) = o;
-    }
-  }
-  cp_async_wait_all();  // the rotation scales of the stage (issued before its barrier)
   __syncthreads();
+}
+
+__device__ __forceinline__ void stage_input(const LinearStage& L, int b0, int rows, int c0, int cols, uint16_t* xin,
+                                            float* red, const unsigned char* smem) {
+  if (L.in_kind == kInRmsNorm) {
+    if (L.in[0].acc) stage_input_k<kInRmsNorm, true>(L, b0, rows, c0, cols, xin, red, smem);
+    else stage_input_k<kInRmsNorm, false>(L, b0, rows, c0, cols, xin, red, smem);
+  } else if (L.in_kind == kInSiluMul) {
+    stage_input_k<kInSiluMul, true>(L, b0, rows, c0, cols, xin, red, smem);
+  } else {
+    stage_input_k<kInPlain, false>(L, b0, rows, c0, cols, xin, red, smem);
+  }
+}
+
+// x of one rotation input chunk: the staged value, normed for RMS-norm stages
+__device__ __forceinline__ void rot_input8(const LinearStage& L, uint4 xv, const uint16_t* gam, float r, float* v) {
+  unpack8(xv, v);
+  if (L.in_kind == kInRmsNorm) {
+    float g[8];
+    unpack8(*reinterpret_cast<const uint4*>(gam), g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = r16(g[e] * r16(v[e] * r));
+  }
 }
 
 template <int HB>
@@ -344,25 +440,19 @@ __device__ __forceinline__ void step_column_pass(const float* scr, __half* z, in
 
 // z rows [b0, b0+rows) of one op: FWHT(xin * rot_scale) per Hadamard block.
 __device__ __forceinline__ void stage_rotate(const LinearStage& L, const uint16_t* rs, const uint16_t* xin, int rows, int c0,
-                             int cols, float* scr, __half* z, int zst) {
+                             int cols, float* scr, __half* z, int zst, const uint16_t* gam, const float* rinv) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lg = L.lg_block, tpr = cols >> 8;
   for (int k = warp; k < rows * tpr; k += kStepWarps) {
     const int rr = k / tpr, cl = (k - rr * tpr) * 256 + lane * 8;
-    float v[8];
-    const uint4 xv = *reinterpret_cast<const uint4*>(xin + rr * cols + cl);
-    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    float v[8], rf[8];
+    rot_input8(L, *reinterpret_cast<const uint4*>(xin + rr * cols + cl), gam + cl, rinv[rr], v);
     // slice-local scales (shared memory: zero past d; global: guarded)
     uint4 rv = make_uint4(0u, 0u, 0u, 0u);
     if (L.rs_smem || c0 + cl < L.d) rv = *reinterpret_cast<const uint4*>(rs + cl);
-    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+    unpack8(rv, rf);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
-      const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[e]));
-      v[2 * e] = xf.x * rf.x;
-      v[2 * e + 1] = xf.y * rf.y;
-    }
+    for (int e = 0; e < 8; ++e) v[e] *= rf[e];
     fwht_regs<3>(v);
 #pragma unroll
     for (int sbit = 0; sbit < 5; ++sbit) {
@@ -400,7 +490,7 @@ __device__ __forceinline__ void stage_rotate(const LinearStage& L, const uint16_
 template <int E>
 __device__ __forceinline__ void rotate_small_blocks(const LinearStage& L, const uint16_t* rs_all, int rs_stride,
                                                     const uint16_t* xin, int rows, int b0, int B, int c0, int cols,
-                                                    __half* z, int zst) {
+                                                    __half* z, int zst, const uint16_t* gam, const float* rinv) {
   constexpr int LGE = E == 16 ? 4 : 3;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int blk = 32 * E, nblk = cols / blk, per_op = rows * nblk;
@@ -411,17 +501,14 @@ __device__ __forceinline__ void rotate_small_blocks(const LinearStage& L, const 
     float v[E];
 #pragma unroll
     for (int q = 0; q < E / 8; ++q) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(xin + rr * cols + cl + 8 * q);
+      float rf[8];
+      rot_input8(L, *reinterpret_cast<const uint4*>(xin + rr * cols + cl + 8 * q), gam + cl + 8 * q, rinv[rr],
+                 v + 8 * q);
       uint4 rv = make_uint4(0u, 0u, 0u, 0u);
       if (L.rs_smem || c0 + cl + 8 * q < L.d) rv = *reinterpret_cast<const uint4*>(rs + cl + 8 * q);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      unpack8(rv, rf);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
-        const float2 rf = __half22float2(*reinterpret_cast<const __half2*>(&rw[e]));
-        v[8 * q + 2 * e] = xf.x * rf.x;
-        v[8 * q + 2 * e + 1] = xf.y * rf.y;
-      }
+      for (int e = 0; e < 8; ++e) v[8 * q + e] *= rf[e];
     }
     fwht_regs<LGE>(v);
 #pragma unroll
@@ -437,26 +524,47 @@ __device__ __forceinline__ void rotate_small_blocks(const LinearStage& L, const 
   __syncthreads();
 }
 
-// Rotation scales of a linear stage into shared memory (cp.async, waited for
-// in stage_input): issued before the barrier that precedes the stage, they
-// depend on nothing the barrier orders.
-__device__ void stage_rs_prefetch(const LinearStage& L, unsigned char* smem) {
+// Static vectors of a linear stage into shared memory (cp.async, one commit
+// group, waited for in stage_input): every op's rotation scales, the norm
+// weight and the producer scales of accumulator inputs.  Issued before the
+// barrier that precedes the stage: they depend on nothing it orders.
+__device__ void stage_static_prefetch(const LinearStage& L, unsigned char* smem) {
   const int slice = blockIdx.x / L.cps;
-  if (slice >= L.kparts || !L.rs_smem) return;
-  const int Us = L.split[slice == L.kparts - 1 ? 1 : 0].us;
-  const int cols = Us * kUnitCols, c0 = slice * L.us * kUnitCols;
-  uint16_t* rs_s = reinterpret_cast<uint16_t*>(smem + L.rs_off);
-  for (int i = threadIdx.x; i < L.nops * (cols / 8); i += kStepThreads) {
-    const int k = i / (cols / 8), ci = i - k * (cols / 8);
-    const bool valid = c0 + ci * 8 < L.d;
-    cp_async16(rs_s + k * cols + ci * 8, L.ops[k].rot_scale + (valid ? c0 + ci * 8 : 0), valid);
+  if (slice < L.kparts) {
+    const int Us = L.split[slice == L.kparts - 1 ? 1 : 0].us;
+    const int cols = Us * kUnitCols, c0 = slice * L.us * kUnitCols, n8 = cols / 8;
+    uint16_t* rs_s = reinterpret_cast<uint16_t*>(smem + L.rs_off);
+    uint16_t* gam_s = reinterpret_cast<uint16_t*>(smem + L.gam_off);
+    uint16_t* psc_s = reinterpret_cast<uint16_t*>(smem + L.psc_off);
+    const bool gam = L.in_kind == kInRmsNorm;
+    const int nrs = L.rs_smem ? L.nops : 0;
+    const int nv = nrs + (gam ? 1 : 0) + L.nin;
+    for (int i = threadIdx.x; i < nv * n8; i += kStepThreads) {
+      const int k = i / n8, ci = i - k * n8, c = c0 + ci * 8;
+      const bool valid = c < L.d;
+      const uint16_t* src;
+      uint16_t* dst;
+      if (k < nrs) {
+        src = L.ops[k].rot_scale;
+        dst = rs_s + k * cols;
+      } else if (gam && k == nrs) {
+        src = L.gamma;
+        dst = gam_s;
+      } else {
+        const int j = k - nrs - (gam ? 1 : 0);
+        src = L.in[j].scale;
+        dst = psc_s + j * cols;
+      }
+      cp_async16(dst + ci * 8, src + (valid ? c : 0), valid);
+    }
   }
+  cp_async_commit();
 }
 
 // Stage prologue: rotation scales to shared memory (async), the input
 // transform, every op's rotated activations, and the zero rows (CTAs of a
 // K-slice: the slice's columns).
-__device__ __forceinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
+__device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
   const int tid = threadIdx.x;
   const int slice = blockIdx.x / L.cps;
   if (slice >= L.kparts) return;
@@ -467,17 +575,19 @@ __device__ __forceinline__ void stage_prologue(const LinearStage& L, unsigned ch
   uint16_t* xin = reinterpret_cast<uint16_t*>(smem + L.xin_off);
   float* scr = reinterpret_cast<float*>(smem + L.scr_off);
   uint16_t* rs_s = reinterpret_cast<uint16_t*>(smem + L.rs_off);
+  const uint16_t* gam = reinterpret_cast<const uint16_t*>(smem + L.gam_off);
+  const float* rinv = red + kStepMaxBatch * kStepWarps;
   for (int b0 = 0; b0 < B; b0 += L.rpp) {
     const int rows = min(L.rpp, B - b0);
-    stage_input(L, b0, rows, c0, cols, xin, red);
+    stage_input(L, b0, rows, c0, cols, xin, red, smem);
     step_mark(4);
     if (L.lg_block <= 9 && L.rs_smem) {
-      if (L.lg_block == 9) rotate_small_blocks<16>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
-      else rotate_small_blocks<8>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst);
+      if (L.lg_block == 9) rotate_small_blocks<16>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst, gam, rinv);
+      else rotate_small_blocks<8>(L, rs_s, cols, xin, rows, b0, B, c0, cols, z, zst, gam, rinv);
     } else {
       for (int k = 0; k < L.nops; ++k)
         stage_rotate(L, L.rs_smem ? rs_s + k * cols : L.ops[k].rot_scale + c0, xin, rows, c0, cols, scr,
-                     z + (k * (B + 1) + b0) * zst, zst);
+                     z + (k * (B + 1) + b0) * zst, zst, gam, rinv);
     }
   }
   step_mark(5);
@@ -489,8 +599,8 @@ __device__ __forceinline__ void stage_prologue(const LinearStage& L, unsigned ch
 }
 
 template <int BITS>
-__device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
-                             unsigned char* ws, const StepHeader& H, int sidx) {
+__device__ __noinline__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
+                                             int sidx) {
   constexpr int S = 64;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -548,66 +658,20 @@ __device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char
   const int src = (lane & ~3) | ((t + 3) & 3);
   const int64_t row_skip = (int64_t)(L.units_k - Us) * UB;
   const unsigned char* wp = unit_ptr(opk, rt, ul) + lane * BITS * 16;
-  unsigned* counters = reinterpret_cast<unsigned*>(ws + kWsCounters);
-  float* part = reinterpret_cast<float*>(ws + H.ws_part_off);
-
+  // a finished (row tile, K range): its raw sums are added to the op's fp32
+  // accumulator (red.add, no ordering needed before the stage's barrier)
   auto flush = [&](int frt, int k) {
-    float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = acc[0][e] + acc[1][e];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
-    const bool solo = L.kparts == 1 && j0 <= frt * Us && (frt + 1) * Us <= j1;
     step_mark(6);
-    if (!solo) {
-      const int rank = wl - sp.warp_of(frt * Us);
-      float* pc = part + ((int64_t)(frt * L.kparts + slice) * L.maxc + rank) * 16 * B;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int col = 2 * t + (e & 1), row = g + 8 * (e >> 1);
-        if (col < B) __stcg(pc + row * B + col, v[e]);
-      }
-      __threadfence();
-      __syncwarp();
-      const SliceSplit& s0 = L.split[0];
-      const SliceSplit& s1 = L.split[1];
-      const int c0_ = s0.warp_of((frt + 1) * s0.us - 1) - s0.warp_of(frt * s0.us) + 1;
-      const int c1_ = s1.warp_of((frt + 1) * s1.us - 1) - s1.warp_of(frt * s1.us) + 1;
-      unsigned last = 0u;
-      if (lane == 0)
-        last = atomicAdd(&counters[frt], 1u) == (unsigned)((L.kparts - 1) * c0_ + c1_ - 1) ? 1u : 0u;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) return;
-      step_mark(7);
-      __threadfence();
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = 0.f;
-      for (int sl = 0; sl < L.kparts; ++sl) {
-        const int cnt = sl == L.kparts - 1 ? c1_ : c0_;
-        const float* pp = part + (int64_t)(frt * L.kparts + sl) * L.maxc * 16 * B;
-        for (int kk = 0; kk < cnt; ++kk, pp += 16 * B) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int col = 2 * t + (e & 1), row = g + 8 * (e >> 1);
-            if (col < B) v[e] += __ldcg(pp + row * B + col);
-          }
-        }
-      }
-      if (lane == 0) counters[frt] = 0u;
-    }
     const StepOp& op = L.ops[k];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
+      const float v = acc[0][e] + acc[1][e];
       const int col = 2 * t + (e & 1);
       const int row = (frt - op.rt_off) * kTileRows + g + 8 * (e >> 1);
-      if (col < B && row < op.n) {
-        float o = v[e] * h2f(op.scales[row]);
-        if (op.bias) o += h2f(op.bias[row]);
-        uint16_t* dst = op.out + (int64_t)col * op.n + row;
-        if (L.epi == kEpiResidual) o = h2f(*dst) + r16(o);
-        *dst = f2h(o);
-      }
+      if (col < B && row < op.n) atomicAdd(op.acc + (int64_t)col * op.n + row, v);
     }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
   };
 
   uint4 zv = make_uint4(0u, 0u, 0u, 0u);
@@ -703,20 +767,18 @@ __device__ __forceinline__ void head_norm(float* x, const float* gam, int hd, fl
 }
 
 // RoPE (rotate-half form) on a head vector (E values per lane, lanes 0-15
-// hold the first half): fp16(fp16(x*cos) + fp16(rot*sin)), cos / sin of
-// pos * inv_freq rounded to fp16.
+// hold the first half): fp16(fp16(x*cos) + fp16(rot*sin)) with the fp16 cos /
+// sin of the fp32 angle pos * inv_freq (c, s: this lane's E values).
 template <int E>
-__device__ __forceinline__ void rope(float* x, const float* freq, int pos, int lane) {
+__device__ __forceinline__ void rope(float* x, const float* c, const float* sn, int lane) {
   float partner[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
   const bool hi = lane >= 16;
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const float f = (float)pos * freq[e];
-    const float c = r16(cosf(f)), s = r16(sinf(f));
     const float rot = hi ? partner[e] : -partner[e];
-    x[e] = r16(r16(x[e] * c) + r16(rot * s));
+    x[e] = r16(r16(x[e] * c[e]) + r16(rot * sn[e]));
   }
 }
 
@@ -732,10 +794,71 @@ __device__ __forceinline__ void load_h(float* v, const uint16_t* p) {
     v[0] = a.x, v[1] = a.y;
   }
 }
+// E fp16 values as raw bits (one 8- or 4-byte load), converted later
+template <int E>
+struct HRaw {
+  uint32_t w[E / 2];
+};
+template <int E>
+__device__ __forceinline__ HRaw<E> ld_hraw(const uint16_t* p) {
+  HRaw<E> r;
+  if constexpr (E == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    r.w[0] = v.x, r.w[1] = v.y;
+  } else {
+    r.w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+  return r;
+}
+template <int E>
+__device__ __forceinline__ void cvt_hraw(const HRaw<E>& r, float* v) {
+#pragma unroll
+  for (int i = 0; i < E / 2; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.w[i]));
+    v[2 * i] = f.x, v[2 * i + 1] = f.y;
+  }
+}
 
+// One head vector of a projection output from its accumulator: E values of
+// r16(acc * scale + bias) at column `col` of batch row b.
+template <int E>
+struct ProjRaw {
+  float a[E];
+  HRaw<E> sc, bi;
+};
+template <int E>
+__device__ __forceinline__ void proj_load(const InVec& V, int64_t row_off, int col, ProjRaw<E>& r) {
+  if constexpr (E == 4) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(V.acc + row_off + col));
+    r.a[0] = v.x, r.a[1] = v.y, r.a[2] = v.z, r.a[3] = v.w;
+  } else {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(V.acc + row_off + col));
+    r.a[0] = v.x, r.a[1] = v.y;
+  }
+  r.sc = ld_hraw<E>(V.scale + col);
+  if (V.bias) r.bi = ld_hraw<E>(V.bias + col);
+}
+template <int E>
+__device__ __forceinline__ void proj_finish(const InVec& V, const ProjRaw<E>& r, float* x) {
+  float sc[E], bi[E];
+  cvt_hraw<E>(r.sc, sc);
+  if (V.bias) cvt_hraw<E>(r.bi, bi);
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = r16(V.bias ? r.a[e] * sc[e] + bi[e] : r.a[e] * sc[e]);
+}
+
+constexpr int kTok = 4;  // cached tokens per warp in flight
+
+// One attention item: batch row b, kv head kvh, split sp of the positions
+// [0, pos]: the q heads of the group (head norm, RoPE), the new token's k / v
+// (appended to the caches by the split that owns position pos), an online
+// softmax per warp over its tokens (kTok in flight, the next kTok loading
+// while these are used), the warps combined in shared memory, the split's
+// (max, sum, weighted values) written to the workspace; the last split of the
+// group to finish combines all splits into the fp16 output.
 template <int E, int G>
-__device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, unsigned char* buf, float* part,
-                          unsigned* counters, int cgroup, unsigned* s_last) {
+__device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, unsigned char* buf,
+                                          float* part, unsigned* counters, int cgroup, unsigned* s_last) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hd = A.hd, gs = A.q_heads / A.kv_heads;
   float* sq = reinterpret_cast<float*>(buf);                 // [gs][hd] normed, roped q
@@ -745,32 +868,62 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   const int T = pos + 1, Ls = (T + A.nsplit - 1) / A.nsplit;
   const int t0 = sp * Ls, t1 = min(T, t0 + Ls);
   const int64_t kv0 = ((int64_t)b * A.kv_heads + kvh) * A.max_t;
-  // this warp's first cached token, loaded before anything waits
-  float kx[E], vx[E];
-  int tok = t0 + warp;
-  if (tok < t1 && tok != pos) {
-    load_h<E>(kx, A.k_cache + (kv0 + tok) * hd + lane * E);
-    load_h<E>(vx, A.v_cache + (kv0 + tok) * hd + lane * E);
-  }
+  // this warp's first cached tokens, loaded before anything waits
+  HRaw<E> kr[kTok], vr[kTok];
+  auto load_tokens = [&](int first) {
+#pragma unroll
+    for (int i = 0; i < kTok; ++i) {
+      const int tk = first + i * kStepWarps;
+      if (tk < t1 && tk != pos) {
+        kr[i] = ld_hraw<E>(A.k_cache + (kv0 + tk) * hd + lane * E);
+        vr[i] = ld_hraw<E>(A.v_cache + (kv0 + tk) * hd + lane * E);
+      }
+    }
+  };
+  load_tokens(t0 + warp);
   // q heads of the group (one warp per head) and the new token's k / v
   const bool newtok = t1 == T && t0 < t1;
   if (warp < gs || (warp == kStepWarps - 1 && newtok)) {
     const bool isq = warp < gs;
-    const uint16_t* src = isq ? A.q + (int64_t)b * A.q_heads * hd + (kvh * gs + warp) * hd
-                              : A.k + (int64_t)b * A.kv_heads * hd + kvh * hd;
+    const InVec& P = isq ? A.q : A.k;
+    const int col = (isq ? (kvh * gs + warp) * hd : kvh * hd) + lane * E;
+    const int64_t ro = (int64_t)b * (isq ? A.q_heads : A.kv_heads) * hd;
     const uint16_t* gam = isq ? A.q_norm : A.k_norm;
-    float x[E], gm[E], fr[E], vv[E];
-    load_h<E>(x, src + lane * E);
-    if (gam) load_h<E>(gm, gam + lane * E);
+    ProjRaw<E> pr, vrw;
+    HRaw<E> gr, cr, sr;
+    proj_load<E>(P, ro, col, pr);
+    if (!isq) proj_load<E>(A.v, ro, col, vrw);
+    if (gam) gr = ld_hraw<E>(gam + lane * E);
+    const int fo = (lane & 15) * E;
+    if (A.rope_cos) {
+      cr = ld_hraw<E>(A.rope_cos + (int64_t)pos * (hd / 2) + fo);
+      sr = ld_hraw<E>(A.rope_sin + (int64_t)pos * (hd / 2) + fo);
+    }
+    float x[E], c[E], sn[E];
+    proj_finish<E>(P, pr, x);
+    if (A.rope_cos) {
+      cvt_hraw<E>(cr, c);
+      cvt_hraw<E>(sr, sn);
+    } else {
 #pragma unroll
-    for (int e = 0; e < E; ++e) fr[e] = A.inv_freq[(lane & 15) * E + e];
-    if (!isq) load_h<E>(vv, A.v + (int64_t)b * A.kv_heads * hd + kvh * hd + lane * E);
-    if (gam) head_norm<E>(x, gm, hd, A.eps);
-    rope<E>(x, fr, pos, lane);
+      for (int e = 0; e < E; ++e) {
+        const float f = (float)pos * A.inv_freq[fo + e];
+        c[e] = r16(cosf(f));
+        sn[e] = r16(sinf(f));
+      }
+    }
+    if (gam) {
+      float gm[E];
+      cvt_hraw<E>(gr, gm);
+      head_norm<E>(x, gm, hd, A.eps);
+    }
+    rope<E>(x, c, sn, lane);
     if (isq) {
 #pragma unroll
       for (int e = 0; e < E; ++e) sq[warp * hd + lane * E + e] = x[e];
     } else {
+      float vv[E];
+      proj_finish<E>(A.v, vrw, vv);
       const int64_t ci = (kv0 + pos) * hd;
 #pragma unroll
       for (int e = 0; e < E; ++e) {
@@ -784,47 +937,57 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   __syncthreads();
   step_mark(4);
   // per-warp online softmax over its tokens
-  float qv[G][E], m[G], l[G], acc[G][E];
+  float m[G], l[G], acc[G][E];
 #pragma unroll
   for (int j = 0; j < G; ++j) {
     m[j] = -INFINITY;
     l[j] = 0.f;
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      qv[j][e] = j < gs ? sq[j * hd + lane * E + e] : 0.f;
-      acc[j][e] = 0.f;
-    }
+    for (int e = 0; e < E; ++e) acc[j][e] = 0.f;
   }
-  for (; tok < t1; tok += kStepWarps) {
-    if (tok == pos) {
+  for (int first = t0 + warp; first < t1; first += kTok * kStepWarps) {
+    float kx[kTok][E], vx[kTok][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) kx[e] = knew[lane * E + e], vx[e] = vnew[lane * E + e];
+    for (int i = 0; i < kTok; ++i) {
+      const int tk = first + i * kStepWarps;
+      if (tk == pos) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) kx[i][e] = knew[lane * E + e], vx[i][e] = vnew[lane * E + e];
+      } else {
+        cvt_hraw<E>(kr[i], kx[i]);
+        cvt_hraw<E>(vr[i], vx[i]);
+      }
     }
-    // next token's k / v in flight while this one is used
-    float kn[E], vn[E];
-    const int nt = tok + kStepWarps;
-    if (nt < t1 && nt != pos) {
-      load_h<E>(kn, A.k_cache + (kv0 + nt) * hd + lane * E);
-      load_h<E>(vn, A.v_cache + (kv0 + nt) * hd + lane * E);
+    // the next tokens load while these are used
+    load_tokens(first + kTok * kStepWarps);
+#pragma unroll
+    for (int i = 0; i < kTok; ++i) {
+      if (first + i * kStepWarps >= t1) break;
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        if (j >= gs) break;
+        float qv[E];
+        if constexpr (E == 4) {
+          const float4 q4 = *reinterpret_cast<const float4*>(sq + j * hd + lane * 4);
+          qv[0] = q4.x, qv[1] = q4.y, qv[2] = q4.z, qv[3] = q4.w;
+        } else {
+          const float2 q2 = *reinterpret_cast<const float2*>(sq + j * hd + lane * 2);
+          qv[0] = q2.x, qv[1] = q2.y;
+        }
+        float sc = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) sc = fmaf(qv[e], kx[i][e], sc);
+        for (int o = 16; o; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
+        sc = r16(r16(sc) * A.scaling);
+        const float mn = fmaxf(m[j], sc);
+        const float corr = __expf(m[j] - mn), p = __expf(sc - mn);
+        l[j] = l[j] * corr + p;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[i][e]);
+        m[j] = mn;
+      }
     }
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      if (j >= gs) break;
-      float sc = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) sc = fmaf(qv[j][e], kx[e], sc);
-      for (int o = 16; o; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-      // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
-      sc = r16(r16(sc) * A.scaling);
-      const float mn = fmaxf(m[j], sc);
-      const float corr = __expf(m[j] - mn), p = __expf(sc - mn);
-      l[j] = l[j] * corr + p;
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[e]);
-      m[j] = mn;
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) kx[e] = kn[e], vx[e] = vn[e];
   }
   step_mark(5);
   // combine the warps
@@ -864,35 +1027,52 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   step_mark(6);
   if (!*s_last) return;
   __threadfence();
+  // warp w: head j = w % gs, a 1 / (16 / gs) share of its columns; lane s
+  // holds split s's max and sum, every lane its columns of all splits (all
+  // loads in flight at once)
   const float* gp = part + (int64_t)cgroup * A.nsplit * gs * ws_;
-  // split maxima and sums into shared memory first (one pass of loads)
-  float* ml = wst;  // [nsplit][gs][2]
-  for (int i = tid; i < A.nsplit * gs; i += kStepThreads) {
-    ml[2 * i] = __ldcg(gp + i * ws_);
-    ml[2 * i + 1] = __ldcg(gp + i * ws_ + 1);
+  const int wph = kStepWarps / gs, j = warp % gs, quarter = warp / gs;
+  const int per = hd / wph;  // columns per warp: 8 .. 64
+  const int dd0 = quarter * per;
+  constexpr int kC = 16;  // splits per pass
+  float M = -INFINITY;
+  float ms = -INFINITY, ls = 0.f;
+  if (lane < A.nsplit) {
+    ms = __ldcg(gp + (lane * gs + j) * ws_);
+    ls = __ldcg(gp + (lane * gs + j) * ws_ + 1);
   }
-  __syncthreads();
-  step_mark(1);
-  for (int i = tid; i < gs * hd; i += kStepThreads) {
-    const int j = i / hd, dd = i - j * hd;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < A.nsplit; ++s2) M = fmaxf(M, ml[2 * (s2 * gs + j)]);
-    // every split's partial in flight at once, then the weighted sum
-    float av[kMaxSplits];
+  float av[kC][2];
+  auto load_av = [&](int s0) {
 #pragma unroll
-    for (int s2 = 0; s2 < kMaxSplits; ++s2)
-      if (s2 < A.nsplit) av[s2] = __ldcg(gp + (s2 * gs + j) * ws_ + 2 + dd);
-    float Lsum = 0.f, Ad = 0.f;
-#pragma unroll
-    for (int s2 = 0; s2 < kMaxSplits; ++s2) {
-      if (s2 >= A.nsplit) break;
-      const float ms = ml[2 * (s2 * gs + j)];
-      const float f = ms == -INFINITY ? 0.f : __expf(ms - M);
-      Lsum += ml[2 * (s2 * gs + j) + 1] * f;
-      Ad += av[s2] * f;
+    for (int s2 = 0; s2 < kC; ++s2) {
+      if (s0 + s2 < A.nsplit) {
+        const float* src = gp + ((s0 + s2) * gs + j) * ws_ + 2 + dd0;
+        av[s2][0] = lane < per ? __ldcg(src + lane) : 0.f;
+        av[s2][1] = lane + 32 < per ? __ldcg(src + lane + 32) : 0.f;
+      }
     }
-    A.out[(int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd] = f2h(Ad / Lsum);
+  };
+  load_av(0);
+  M = ms;
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float fs = ms == -INFINITY ? 0.f : __expf(ms - M);
+  float Lsum = fs * ls;
+  for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+  float o0 = 0.f, o1 = 0.f;
+  for (int s0 = 0; s0 < A.nsplit; s0 += kC) {
+    if (s0 > 0) load_av(s0);
+#pragma unroll
+    for (int s2 = 0; s2 < kC; ++s2) {
+      const float f = __shfl_sync(0xffffffffu, fs, (s0 + s2) & 31);
+      if (s0 + s2 < A.nsplit) {
+        o0 = fmaf(f, av[s2][0], o0);
+        o1 = fmaf(f, av[s2][1], o1);
+      }
+    }
   }
+  uint16_t* dst = A.out + (int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd0;
+  if (lane < per) dst[lane] = f2h(o0 / Lsum);
+  if (lane + 32 < per) dst[lane + 32] = f2h(o1 / Lsum);
   step_mark(7);
   if (tid == 0) counters[cgroup] = 0u;
 }
@@ -940,14 +1120,26 @@ __device__ void prefetch_attention(const AttnStage& A, int B, int pos) {
   }
 }
 
-__device__ void final_norm_stage(const NormStage& N, int B, float* red) {
+// Final stage: h = r16(base + r16(acc * scale + bias)) (the last down_proj
+// added to the residual), written to hout; out = r16(gamma * r16(h * rinv)).
+// One CTA per batch row; it also clears the row of the accumulator it read.
+__device__ void final_norm_stage(const NormStage& N, int B, float* red, uint16_t* hbuf) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    const uint16_t* x = N.x + (int64_t)b * N.d;
+    const int64_t ro = (int64_t)b * N.d;
     float s = 0.f;
-    for (int c = tid; c < N.d; c += kStepThreads) {
-      const float f = h2f(x[c]);
-      s += f * f;
+    for (int c = tid * 8; c < N.d; c += kStepThreads * 8) {
+      ChunkRaw r;
+      load_chunk<true, true>(N.x, ro, c, r);
+      float f[8];
+      finish_chunk<true, true>(N.x, r, N.x.scale, c, c, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(f[e], f[e], s);
+      *reinterpret_cast<uint4*>(hbuf + c) = pack8(f);
+      if (N.x.acc) {
+        __stcg(reinterpret_cast<float4*>(const_cast<float*>(N.x.acc) + ro + c), make_float4(0.f, 0.f, 0.f, 0.f));
+        __stcg(reinterpret_cast<float4*>(const_cast<float*>(N.x.acc) + ro + c + 4), make_float4(0.f, 0.f, 0.f, 0.f));
+      }
     }
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) red[warp] = s;
@@ -955,8 +1147,28 @@ __device__ void final_norm_stage(const NormStage& N, int B, float* red) {
     float tot = 0.f;
     for (int w = 0; w < kStepWarps; ++w) tot += red[w];
     const float r = rsqrtf(tot / (float)N.d + N.eps);
-    for (int c = tid; c < N.d; c += kStepThreads) N.out[(int64_t)b * N.d + c] = f2h(h2f(N.gamma[c]) * r16(h2f(x[c]) * r));
+    for (int c = tid * 8; c < N.d; c += kStepThreads * 8) {
+      float h[8], g[8], o[8];
+      const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + c);
+      unpack8(hv, h);
+      unpack8(*reinterpret_cast<const uint4*>(N.gamma + c), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = r16(g[e] * r16(h[e] * r));
+      *reinterpret_cast<uint4*>(N.hout + ro + c) = hv;
+      *reinterpret_cast<uint4*>(N.out + ro + c) = pack8(o);
+    }
     __syncthreads();
+  }
+}
+
+// every CTA clears its share (16-byte stores, grid-stride) of the stage's
+// zero list
+__device__ __forceinline__ void stage_zero(const StepStage& st) {
+  for (int z = 0; z < st.nzero; ++z) {
+    float4* p = reinterpret_cast<float4*>(st.zero_ptr[z]);
+    const int64_t n = st.zero_bytes[z] / 16;
+    for (int64_t i = (int64_t)blockIdx.x * kStepThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kStepThreads)
+      __stcg(p + i, make_float4(0.f, 0.f, 0.f, 0.f));
   }
 }
 
@@ -995,15 +1207,21 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   float* red = reinterpret_cast<float*>(smem + H.misc_off + kMiscRed);
   const uint16_t* cur_cb = nullptr;
   int cur_bits = 0;
+  if (blockIdx.x == 0 && tid == 0) {
+    reinterpret_cast<int64_t*>(ws + kWsLayout)[0] = H.ws_acc_off;
+    reinterpret_cast<int64_t*>(ws + kWsLayout)[1] = H.ws_acc_bytes;
+  }
   fetch(0);
   fetch(1);
   cp_async_wait_all();
   __syncthreads();
-  if (H.nstages > 0 && slots[0].type == kLinear) stage_rs_prefetch(slots[0].lin, smem);
+  if (H.nstages > 0 && slots[0].type == kLinear) stage_static_prefetch(slots[0].lin, smem);
   for (int s = 0; s < H.nstages; ++s) {
     const StepStage& st = slots[s % 3];
     fetch(s + 2);
+    cp_async_commit();
     step_trace(s, 0);
+    stage_zero(st);
     if (s + 1 < H.nstages && slots[(s + 1) % 3].type == kAttention) prefetch_attention(slots[(s + 1) % 3].attn, H.B, pos);
     if (st.type == kLinear) {
       const LinearStage& L = st.lin;
@@ -1019,13 +1237,13 @@ __global__ void __launch_bounds__(kStepThreads, 1)
       }
       stage_prologue(L, smem, H.B, red);
       step_trace(s, 1);
-      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, ws, H, s);
-      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, ws, H, s);
-      else linear_stage<4>(L, smem, H.B, lut4, ws, H, s);
+      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, s);
+      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, s);
+      else linear_stage<4>(L, smem, H.B, lut4, s);
     } else if (st.type == kAttention) {
       attn_stage(st.attn, H.B, pos, smem, ws, H);
     } else {
-      final_norm_stage(st.fnorm, H.B, red);
+      final_norm_stage(st.fnorm, H.B, red, reinterpret_cast<uint16_t*>(smem + st.fnorm.buf_off));
     }
     step_trace(s, 2);
     if (s + 1 == H.nstages) break;
@@ -1034,7 +1252,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     const StepStage& nx = slots[(s + 1) % 3];
     if (nx.type == kLinear) {
       prefetch_stage(nx.lin);
-      stage_rs_prefetch(nx.lin, smem);
+      stage_static_prefetch(nx.lin, smem);
     }
     if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x + (unsigned)H.extra_arrivals, limit_ns, s_ok)) break;
     step_trace(s, 3);
@@ -1064,9 +1282,25 @@ bool valid_linear(const tp_step_linear& l) {
          l.d % l.block == 0 && aligned(l.tcq_stream, 16) && aligned(l.rot_scale, 16);
 }
 
-// Plan one linear stage (ops share d, block, bits, codebook).
-tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t* const* outs, int nops, int B,
-                      int G, const Regions& R, int64_t* rt_max, int64_t* part_floats) {
+// Shared-memory buffer sizes of a linear stage for K-slices of `cols`
+// columns and rpp rows per pass: activations z, input rows, fp32 scratch,
+// rotation scales, norm weight, producer scales.
+void linear_sizes(const LinearStage& L, int B, int cols, int rpp, int rs_smem, uint32_t* sz) {
+  const bool need_scr = !(rs_smem && L.lg_block <= 9);
+  auto r128 = [](int64_t v) { return static_cast<uint32_t>((v + 127) / 128 * 128); };
+  sz[0] = r128((int64_t)L.nops * (B + 1) * (cols + kZPad) * 2);
+  sz[1] = r128((int64_t)rpp * cols * 2);
+  sz[2] = need_scr ? r128((int64_t)rpp * cols * 4) : 0u;
+  sz[3] = r128((int64_t)rs_smem * L.nops * cols * 2);
+  sz[4] = L.in_kind == kInRmsNorm ? r128((int64_t)cols * 2) : 0u;
+  sz[5] = r128((int64_t)L.nin * cols * 2);
+}
+constexpr int kBufs = 6;
+
+// Plan one linear stage (ops share d, block, bits, codebook); the input
+// description (in_kind, in[], nin) is set by the caller before.
+tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* const* accs, int nops, int B, int G,
+                      const Regions& R) {
   const tp_step_linear& f = *ops[0];
   for (int k = 0; k < nops; ++k) {
     const tp_step_linear& o = *ops[k];
@@ -1089,10 +1323,8 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
   for (int k = 0; k < nops; ++k) {
     StepOp& op = L.ops[k];
     op.stream = ops[k]->tcq_stream;
-    op.scales = ops[k]->scales;
+    op.acc = accs[k];
     op.rot_scale = ops[k]->rot_scale;
-    op.bias = ops[k]->bias;
-    op.out = outs[k];
     op.n = static_cast<int>(ops[k]->n);
     op.row_tiles = static_cast<int>(pad_to(ops[k]->n, kTileRows) / kTileRows);
     op.rt_off = rt;
@@ -1106,12 +1338,12 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
   // first -- a small shared-memory footprint leaves the SM more L1 -- then
   // to region b (after the table).
   int us = 0, kparts = 0, rpp = 0, rs_smem = 1;
-  uint32_t off[4] = {0, 0, 0, 0};  // z, xin, scr, rs
+  uint32_t off[kBufs] = {0, 0, 0, 0, 0, 0};
   bool found = false;
   auto place = [&](const uint32_t* sz) {
     uint32_t ua = 0, ub = 0;
     const uint32_t ca = R.has4 ? 0 : R.a1 - R.a0, cb = R.b1 - R.b0;
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kBufs; ++i) {
       if (sz[i] == 0) {
         off[i] = R.b0 - R.base;
         continue;
@@ -1136,13 +1368,9 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
       const int kp = (U + us - 1) / us;
       if (kp != kparts) continue;
       const int cols = us * kUnitCols;
-      const bool need_scr = !(rs_smem && L.lg_block <= 9);
       for (rpp = B; rpp >= 1; --rpp) {
-        const uint32_t sz[4] = {
-            static_cast<uint32_t>(((int64_t)nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128),
-            static_cast<uint32_t>(((int64_t)rpp * cols * 2 + 127) / 128 * 128),
-            need_scr ? static_cast<uint32_t>((int64_t)rpp * cols * 4) : 0u,
-            static_cast<uint32_t>((int64_t)rs_smem * nops * cols * 2)};
+        uint32_t sz[kBufs];
+        linear_sizes(L, B, cols, rpp, rs_smem, sz);
         if (place(sz)) {
           found = true;
           break;
@@ -1160,10 +1388,11 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
   L.xin_off = off[1];
   L.scr_off = off[2];
   L.rs_off = off[3];
+  L.gam_off = off[4];
+  L.psc_off = off[5];
   // grid split
   L.cps = std::max(1, G / kparts);
   const int64_t W = (int64_t)L.cps * kStepWarps;
-  L.maxc = 0;
   for (int k = 0; k < 2; ++k) {
     const int64_t su = k == 0 ? us : U - (int64_t)(kparts - 1) * us;
     const int64_t T = (int64_t)rt * su;
@@ -1175,11 +1404,7 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, uint16_t
     L.split[k].div_us = make_fastdiv(static_cast<uint32_t>(su));
     L.split[k].div_r = make_fastdiv(static_cast<uint32_t>(T / Wk));
     L.split[k].div_r1 = make_fastdiv(static_cast<uint32_t>(T / Wk + 1));
-    const int64_t r = T / Wk;
-    L.maxc = std::max<int>(L.maxc, static_cast<int>((su + r - 1) / r + 1));
   }
-  *rt_max = std::max<int64_t>(*rt_max, rt);
-  *part_floats = std::max<int64_t>(*part_floats, (int64_t)rt * kparts * L.maxc * 16 * B);
   return TP_OK;
 }
 
@@ -1198,9 +1423,10 @@ extern "C" int64_t tp_step_image_bytes(int layers) {
 
 extern "C" int64_t tp_step_act_bytes(const tp_step_model* m) {
   if (!m || m->B < 1) return -1;
-  const int64_t qd = (int64_t)m->q_heads * m->head_dim, kd = (int64_t)m->kv_heads * m->head_dim;
-  // q, k, v, attn, gate, up (fp16), each 256-byte aligned
-  return 2 * m->B * (align256(qd) + 2 * align256(kd) + align256(qd) + 2 * align256(m->inter)) + 6 * 256;
+  const int64_t qd = (int64_t)m->q_heads * m->head_dim;
+  // the attention output (fp16 [B][q_heads * head_dim]); the linears'
+  // outputs live in the workspace as fp32 accumulators
+  return 2 * m->B * align256(qd) + 256;
 }
 
 extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* layers, void* image_host,
@@ -1210,9 +1436,12 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   if (B < 1 || B > kStepMaxBatch) return fail(TP_ERR_UNSUPPORTED, "tp_step: batch must be 1..%d", kStepMaxBatch);
   if (m->layers < 1 || image_bytes < tp_step_image_bytes(m->layers))
     return fail(TP_ERR_ARG, "tp_step_build: image buffer too small");
-  if (!(m->head_dim == 128 || m->head_dim == 64) || m->q_heads % m->kv_heads || m->q_heads / m->kv_heads > kMaxGroup)
-    return fail(TP_ERR_UNSUPPORTED, "tp_step: head_dim must be 64 or 128 with at most %d query heads per kv head",
-                kMaxGroup);
+  const int gsz = m->kv_heads > 0 ? m->q_heads / m->kv_heads : 0;
+  if (!(m->head_dim == 128 || m->head_dim == 64) || m->kv_heads < 1 || m->q_heads % m->kv_heads || gsz > kMaxGroup ||
+      (gsz & (gsz - 1)))
+    return fail(TP_ERR_UNSUPPORTED,
+                "tp_step: head_dim must be 64 or 128 with 1, 2, 4 or %d query heads per kv head", kMaxGroup);
+  if (m->hidden % 8 || m->inter % 8) return fail(TP_ERR_UNSUPPORTED, "tp_step: hidden and inter must be multiples of 8");
   if (!m->hidden_state || !m->final_out || !m->final_norm || !m->act || !m->inv_freq || m->max_tokens < 1)
     return fail(TP_ERR_ARG, "tp_step_build: missing buffers");
   int dev = 0, reserved = 0, optin = 0;
@@ -1268,57 +1497,96 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   StepHeader* H = static_cast<StepHeader*>(image_host);
   memset(image_host, 0, static_cast<size_t>(tp_step_image_bytes(m->layers)));
   StepStage* st = reinterpret_cast<StepStage*>(H + 1);
-  const int64_t hd = m->head_dim, qd = m->q_heads * hd, kd = m->kv_heads * hd;
-  unsigned char* act = static_cast<unsigned char*>(m->act);
-  uint16_t* qb = reinterpret_cast<uint16_t*>(act);
-  uint16_t* kb = reinterpret_cast<uint16_t*>(act + B * align256(qd) * 2 + 256);
-  uint16_t* vb = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(kb) + B * align256(kd) * 2 + 256);
-  uint16_t* ab = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(vb) + B * align256(kd) * 2 + 256);
-  uint16_t* gb = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(ab) + B * align256(qd) * 2 + 256);
-  uint16_t* ub = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(gb) + B * align256(m->inter) * 2 + 256);
-  int64_t rt_max = 0, part_floats = 0;
-  int ns = 0;
-  int nsplit = std::min(kMaxSplits, std::max(1, G / (B * m->kv_heads)));
-  const int gs = m->q_heads / m->kv_heads;
-  const uint32_t attn_buf = static_cast<uint32_t>(
-      (kMaxGroup * hd + 2 * hd + kStepWarps * gs * (hd + 2)) * 4);
+  const int64_t hd = m->head_dim, qd = m->q_heads * hd, kd = m->kv_heads * hd, hid = m->hidden, inter = m->inter;
+  uint16_t* ab = reinterpret_cast<uint16_t*>(m->act);  // attention output
+  // workspace: status / barrier / attention counters, attention partials,
+  // fp32 accumulators (one set, reused by every layer), the second residual
+  // buffer
+  const int attn_groups = B * m->kv_heads;
+  int nsplit = std::min(kMaxSplits, std::max(1, G / attn_groups));
+  H->ws_attn_off = align256(kWsCounters + (int64_t)attn_groups * 4);
+  H->ws_acc_off = H->ws_attn_off + align256((int64_t)attn_groups * nsplit * gsz * (hd + 2) * 4);
+  int64_t acc_at = H->ws_acc_off;
+  auto acc_alloc = [&](int64_t n) {
+    const int64_t o = acc_at;
+    acc_at += align256(B * n * 4);
+    return o;
+  };
+  const int64_t o_q = acc_alloc(qd), o_k = acc_alloc(kd), o_v = acc_alloc(kd), o_o = acc_alloc(hid),
+                o_g = acc_alloc(inter), o_u = acc_alloc(inter), o_d = acc_alloc(hid);
+  H->ws_acc_bytes = acc_at - H->ws_acc_off;
+  H->ws_h2_off = acc_at;
+  H->ws_bytes = H->ws_h2_off + align256(B * hid * 2);
+  // device addresses are not known yet: the image holds workspace offsets
+  // in these pointer fields (tagged), patched by tp_step_run
+  auto wsp = [&](int64_t off) { return reinterpret_cast<float*>(static_cast<uintptr_t>(off) | kWsTag); };
+  float *acc_q = wsp(o_q), *acc_k = wsp(o_k), *acc_v = wsp(o_v), *acc_o = wsp(o_o), *acc_g = wsp(o_g),
+        *acc_u = wsp(o_u), *acc_d = wsp(o_d);
+  uint16_t* h2 = reinterpret_cast<uint16_t*>(wsp(H->ws_h2_off));
+  uint16_t* h0 = m->hidden_state;
+  const int gs = gsz;
+  const uint32_t attn_buf = static_cast<uint32_t>((kMaxGroup * hd + 2 * hd + kStepWarps * gs * (hd + 2)) * 4);
   const bool attn_in_a = !has4 && R.a0 + attn_buf <= R.a1;
   const uint32_t attn_at = attn_in_a ? R.a0 : R.b0;
   if (!attn_in_a && R.b0 + attn_buf > R.b1) return fail(TP_ERR_UNSUPPORTED, "tp_step: attention buffers do not fit");
+  int ns = 0;
+  // zero list of a stage: adjacent accumulators merge into one region
+  bool zero_overflow = false;
+  auto zero = [&](StepStage& s, float* p, int64_t n) {
+    const int64_t bytes = align256(B * n * 4);
+    if (s.nzero > 0 && reinterpret_cast<uintptr_t>(s.zero_ptr[s.nzero - 1]) + s.zero_bytes[s.nzero - 1] ==
+                           reinterpret_cast<uintptr_t>(p)) {
+      s.zero_bytes[s.nzero - 1] += bytes;
+      return;
+    }
+    if (s.nzero == 2) {
+      zero_overflow = true;
+      return;
+    }
+    s.zero_ptr[s.nzero] = p;
+    s.zero_bytes[s.nzero] = bytes;
+    ++s.nzero;
+  };
+  const tp_step_linear* prev_down = nullptr;
   for (int i = 0; i < m->layers; ++i) {
     const tp_step_layer& ly = layers[i];
     if (!ly.ln1 || !ly.ln2 || !ly.k_cache || !ly.v_cache) return fail(TP_ERR_ARG, "tp_step: layer %d incomplete", i);
-    if (ly.q.n != qd || ly.k.n != kd || ly.v.n != kd || ly.o.d != qd || ly.o.n != m->hidden || ly.q.d != m->hidden ||
-        ly.gate.n != m->inter || ly.up.n != m->inter || ly.down.d != m->inter || ly.down.n != m->hidden ||
-        ly.gate.d != m->hidden)
+    if (ly.q.n != qd || ly.k.n != kd || ly.v.n != kd || ly.o.d != qd || ly.o.n != hid || ly.q.d != hid ||
+        ly.gate.n != inter || ly.up.n != inter || ly.down.d != inter || ly.down.n != hid || ly.gate.d != hid)
       return fail(TP_ERR_ARG, "tp_step: layer %d shapes do not match the model", i);
-    // QKV
+    // QKV: x = rmsnorm(h), h = h0 (+ the previous layer's down_proj), h written to h2
     {
       StepStage& s = st[ns++];
       s.type = kLinear;
+      LinearStage& L = s.lin;
+      L.in_kind = kInRmsNorm;
+      L.in[0] = InVec{h0, prev_down ? acc_d : nullptr, prev_down ? prev_down->scales : nullptr,
+                      prev_down ? prev_down->bias : nullptr};
+      L.nin = prev_down ? 1 : 0;
+      L.gamma = ly.ln1;
+      L.eps = m->rms_eps;
+      L.hout = h2;
       const tp_step_linear* ops[3] = {&ly.q, &ly.k, &ly.v};
-      uint16_t* outs[3] = {qb, kb, vb};
-      if (tp_status e = plan_linear(s.lin, ops, outs, 3, B, G, R, &rt_max, &part_floats)) return e;
-      s.lin.in_kind = kInRmsNorm;
-      s.lin.in0 = m->hidden_state;
-      s.lin.gamma = ly.ln1;
-      s.lin.eps = m->rms_eps;
-      s.lin.epi = kEpiStore;
+      float* accs[3] = {acc_q, acc_k, acc_v};
+      if (tp_status e = plan_linear(L, ops, accs, 3, B, G, R)) return e;
+      if (i > 0) zero(s, acc_g, inter), zero(s, acc_u, inter);  // read by the previous DOWN
     }
     // ATTN
     {
       StepStage& s = st[ns++];
       s.type = kAttention;
       AttnStage& A = s.attn;
-      A.q = qb;
-      A.k = kb;
-      A.v = vb;
+      A.q = InVec{nullptr, acc_q, ly.q.scales, ly.q.bias};
+      A.k = InVec{nullptr, acc_k, ly.k.scales, ly.k.bias};
+      A.v = InVec{nullptr, acc_v, ly.v.scales, ly.v.bias};
       A.q_norm = ly.q_norm;
       A.k_norm = ly.k_norm;
       A.k_cache = ly.k_cache;
       A.v_cache = ly.v_cache;
       A.out = ab;
       A.inv_freq = m->inv_freq;
+      A.rope_cos = m->rope_cos;
+      A.rope_sin = m->rope_sin;
       A.q_heads = m->q_heads;
       A.kv_heads = m->kv_heads;
       A.hd = m->head_dim;
@@ -1327,67 +1595,76 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
       A.eps = m->rms_eps;
       A.scaling = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)));
       A.buf_off = attn_at - R.base;
+      if (i > 0) zero(s, acc_d, hid);  // read by this layer's QKV
     }
-    // O
+    // O: plain input (the attention output)
     {
       StepStage& s = st[ns++];
       s.type = kLinear;
+      LinearStage& L = s.lin;
+      L.in_kind = kInPlain;
+      L.in[0] = InVec{ab, nullptr, nullptr, nullptr};
+      L.nin = 0;
       const tp_step_linear* ops[1] = {&ly.o};
-      uint16_t* outs[1] = {m->hidden_state};
-      if (tp_status e = plan_linear(s.lin, ops, outs, 1, B, G, R, &rt_max, &part_floats)) return e;
-      s.lin.in_kind = kInPlain;
-      s.lin.in0 = ab;
-      s.lin.epi = kEpiResidual;
+      float* accs[1] = {acc_o};
+      if (tp_status e = plan_linear(L, ops, accs, 1, B, G, R)) return e;
+      zero(s, acc_q, qd), zero(s, acc_k, kd), zero(s, acc_v, kd);  // read by ATTN
     }
-    // GATE / UP
+    // GATE / UP: x = rmsnorm(h2 + o_proj), written back to h0
     {
       StepStage& s = st[ns++];
       s.type = kLinear;
+      LinearStage& L = s.lin;
+      L.in_kind = kInRmsNorm;
+      L.in[0] = InVec{h2, acc_o, ly.o.scales, ly.o.bias};
+      L.nin = 1;
+      L.gamma = ly.ln2;
+      L.eps = m->rms_eps;
+      L.hout = h0;
       const tp_step_linear* ops[2] = {&ly.gate, &ly.up};
-      uint16_t* outs[2] = {gb, ub};
-      if (tp_status e = plan_linear(s.lin, ops, outs, 2, B, G, R, &rt_max, &part_floats)) return e;
-      s.lin.in_kind = kInRmsNorm;
-      s.lin.in0 = m->hidden_state;
-      s.lin.gamma = ly.ln2;
-      s.lin.eps = m->rms_eps;
-      s.lin.epi = kEpiStore;
+      float* accs[2] = {acc_g, acc_u};
+      if (tp_status e = plan_linear(L, ops, accs, 2, B, G, R)) return e;
     }
-    // DOWN
+    // DOWN: x = silu(gate) * up
     {
       StepStage& s = st[ns++];
       s.type = kLinear;
+      LinearStage& L = s.lin;
+      L.in_kind = kInSiluMul;
+      L.in[0] = InVec{nullptr, acc_g, ly.gate.scales, ly.gate.bias};
+      L.in[1] = InVec{nullptr, acc_u, ly.up.scales, ly.up.bias};
+      L.nin = 2;
       const tp_step_linear* ops[1] = {&ly.down};
-      uint16_t* outs[1] = {m->hidden_state};
-      if (tp_status e = plan_linear(s.lin, ops, outs, 1, B, G, R, &rt_max, &part_floats)) return e;
-      s.lin.in_kind = kInSiluMul;
-      s.lin.in0 = gb;
-      s.lin.in1 = ub;
-      s.lin.epi = kEpiResidual;
+      float* accs[1] = {acc_d};
+      if (tp_status e = plan_linear(L, ops, accs, 1, B, G, R)) return e;
+      zero(s, acc_o, hid);  // read by GATE / UP
     }
+    prev_down = &ly.down;
   }
   {
     StepStage& s = st[ns++];
     s.type = kFinalNorm;
-    s.fnorm.x = m->hidden_state;
+    s.fnorm.x = InVec{h0, acc_d, prev_down->scales, prev_down->bias};
     s.fnorm.gamma = m->final_norm;
     s.fnorm.out = m->final_out;
+    s.fnorm.hout = m->hidden_state;
     s.fnorm.d = m->hidden;
     s.fnorm.eps = m->rms_eps;
+    s.fnorm.buf_off = R.b0 - R.base;
+    zero(s, acc_g, inter), zero(s, acc_u, inter);  // read by the last DOWN; acc_d: cleared by the stage itself
   }
+  if (zero_overflow) return fail(TP_ERR_UNSUPPORTED, "tp_step: internal error (zero list)");
   // the largest footprint over the stages sets the dynamic shared memory size
   uint32_t end = std::max<uint32_t>(has4 ? R.b0 : kLutAbs + 65536u, attn_at + attn_buf);
+  end = std::max<uint32_t>(end, R.b0 + static_cast<uint32_t>(hid * 2));
+  if (R.b0 + hid * 2 > R.b1) return fail(TP_ERR_UNSUPPORTED, "tp_step: hidden size too large");
   for (int s = 0; s < ns; ++s) {
     if (st[s].type != kLinear) continue;
     const LinearStage& L = st[s].lin;
-    const int cols = L.us * kUnitCols;
-    const bool need_scr = !(L.rs_smem && L.lg_block <= 9);
-    const uint32_t sz[4] = {
-        static_cast<uint32_t>(((int64_t)L.nops * (B + 1) * (cols + kZPad) * 2 + 127) / 128 * 128),
-        static_cast<uint32_t>(((int64_t)L.rpp * cols * 2 + 127) / 128 * 128),
-        need_scr ? static_cast<uint32_t>((int64_t)L.rpp * cols * 4) : 0u,
-        static_cast<uint32_t>((int64_t)L.rs_smem * L.nops * cols * 2)};
-    const uint32_t offs[4] = {L.z_off, L.xin_off, L.scr_off, L.rs_off};
-    for (int i = 0; i < 4; ++i)
+    uint32_t sz[kBufs];
+    linear_sizes(L, B, L.us * kUnitCols, L.rpp, L.rs_smem, sz);
+    const uint32_t offs[kBufs] = {L.z_off, L.xin_off, L.scr_off, L.rs_off, L.gam_off, L.psc_off};
+    for (int i = 0; i < kBufs; ++i)
       if (sz[i]) end = std::max(end, R.base + offs[i] + sz[i]);
   }
   H->nstages = ns;
@@ -1398,16 +1675,43 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
   H->dyn = end - R.base;
   H->lut_off = has4 ? 0 : kLutAbs - R.base;
   H->misc_off = misc_off;
-  const int attn_groups = B * m->kv_heads;
-  const int64_t counters = std::max<int64_t>(rt_max, attn_groups);
-  H->ws_part_off = align256(kWsCounters + counters * 4);
-  H->ws_attn_off = H->ws_part_off + align256(part_floats * 4);
-  H->ws_bytes = H->ws_attn_off + align256((int64_t)attn_groups * nsplit * gs * (hd + 2) * 4);
-  H->max_rt = static_cast<int>(rt_max);
   H->barrier_us = 0;
   H->extra_arrivals = 0;
   H->attn_groups = attn_groups;
   *workspace_bytes = H->ws_bytes;
+  return clear_ok();
+}
+
+extern "C" tp_status tp_step_bind(void* image_host, void* workspace, int64_t workspace_bytes) {
+  if (!image_host || !workspace) return fail(TP_ERR_ARG, "tp_step_bind: null argument");
+  StepHeader* H = static_cast<StepHeader*>(image_host);
+  if (workspace_bytes < H->ws_bytes)
+    return fail(TP_ERR_WORKSPACE, "tp_step_bind: workspace of %lld bytes required", (long long)H->ws_bytes);
+  if (!aligned(workspace, 256)) return fail(TP_ERR_ALIGN, "tp_step_bind: workspace must be 256-byte aligned");
+  if (H->bound_ws) {
+    if (H->bound_ws == reinterpret_cast<uint64_t>(workspace)) return clear_ok();
+    return fail(TP_ERR_ARG, "tp_step_bind: image already bound to another workspace");
+  }
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  auto fix = [&](auto*& p) {
+    const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+    if (v & kWsTag) p = reinterpret_cast<std::remove_reference_t<decltype(p)>>(ws + (v & ~kWsTag));
+  };
+  StepStage* st = reinterpret_cast<StepStage*>(H + 1);
+  for (int i = 0; i < H->nstages; ++i) {
+    StepStage& S = st[i];
+    for (int z = 0; z < S.nzero; ++z) fix(S.zero_ptr[z]);
+    if (S.type == kLinear) {
+      for (auto& v : S.lin.in) fix(v.base), fix(v.acc);
+      fix(S.lin.hout);
+      for (int k = 0; k < S.lin.nops; ++k) fix(S.lin.ops[k].acc);
+    } else if (S.type == kAttention) {
+      fix(S.attn.q.acc), fix(S.attn.k.acc), fix(S.attn.v.acc);
+    } else {
+      fix(S.fnorm.x.base), fix(S.fnorm.x.acc);
+    }
+  }
+  H->bound_ws = reinterpret_cast<uint64_t>(workspace);
   return clear_ok();
 }
 
@@ -1418,6 +1722,8 @@ extern "C" tp_status tp_step_run(const void* image_dev, const void* image_host, 
   if (workspace_bytes < H->ws_bytes)
     return fail(TP_ERR_WORKSPACE, "tp_step_run: workspace of %lld bytes required", (long long)H->ws_bytes);
   if (!aligned(workspace, 256)) return fail(TP_ERR_ALIGN, "tp_step_run: workspace must be 256-byte aligned");
+  if (H->bound_ws != reinterpret_cast<uint64_t>(workspace))
+    return fail(TP_ERR_ARG, "tp_step_run: the image is not bound to this workspace (tp_step_bind)");
   if (H->grid != step_sm_count()) return fail(TP_ERR_ARG, "tp_step_run: program built for another device");
   int dev = 0;
   TP_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
@@ -1467,7 +1773,18 @@ extern "C" tp_status tp_step_status(const void* workspace, void* stream) {
   TP_CUDA_TRY(cudaMemcpyAsync(&v, ws + kWsStatus, 4, cudaMemcpyDeviceToHost, st), "status copy");
   TP_CUDA_TRY(cudaStreamSynchronize(st), "status sync");
   if (v == 0) return clear_ok();
-  TP_CUDA_TRY(cudaMemsetAsync(const_cast<unsigned char*>(ws) + kWsStatus, 0, 4, st), "status clear");
+  // a step that gave up leaves accumulators and counters part-written: clear
+  // them (and the status) so the next step starts from zero
+  int64_t lay[2] = {0, 0};
+  TP_CUDA_TRY(cudaMemcpyAsync(lay, ws + kWsLayout, sizeof(lay), cudaMemcpyDeviceToHost, st), "layout copy");
+  TP_CUDA_TRY(cudaStreamSynchronize(st), "status sync");
+  unsigned char* w = const_cast<unsigned char*>(ws);
+  TP_CUDA_TRY(cudaMemsetAsync(w + kWsStatus, 0, 4, st), "status clear");
+  if (lay[0] > kWsCounters)  // attention counters and partials
+    TP_CUDA_TRY(cudaMemsetAsync(w + kWsCounters, 0, static_cast<size_t>(lay[0] - kWsCounters), st), "counter clear");
+  if (lay[0] > 0 && lay[1] > 0)
+    TP_CUDA_TRY(cudaMemsetAsync(w + lay[0], 0, static_cast<size_t>(lay[1]), st), "accumulator clear");
+  TP_CUDA_TRY(cudaStreamSynchronize(st), "status sync");
   if (v & kStepStatusLayout) return fail(TP_ERR_DEVICE, "tp_step: shared-memory layout check failed (status %u)", v);
   return fail(TP_ERR_DEVICE, "tp_step: a grid barrier timed out (status %u)", v);
 }

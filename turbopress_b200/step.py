@@ -53,7 +53,8 @@ class _Model(ctypes.Structure):
                 ("inter", ctypes.c_int32), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
                 ("head_dim", ctypes.c_int32), ("max_tokens", ctypes.c_int32), ("rms_eps", ctypes.c_float),
                 ("inv_freq", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("hidden_state", ctypes.c_void_p),
-                ("final_out", ctypes.c_void_p), ("act", ctypes.c_void_p)]
+                ("final_out", ctypes.c_void_p), ("act", ctypes.c_void_p), ("rope_cos", ctypes.c_void_p),
+                ("rope_sin", ctypes.c_void_p)]
 
 
 @dataclass
@@ -117,12 +118,17 @@ class DecodeStep:
         self.final_out = torch.zeros(batch, cfg.hidden, **f16)
         self.final_norm = final_norm.to(**f16).contiguous()
         self.inv_freq = rope_inv_freq(hd, cfg.rope_theta).to(dev)
+        # fp16 cos / sin of the fp32 angles pos * inv_freq, as the reference
+        # model's rotary embedding computes them, for every position
+        ang = torch.arange(max_tokens, device=dev, dtype=torch.float32)[:, None] * self.inv_freq[None, :]
+        self.rope_cos = ang.cos().half().contiguous()
+        self.rope_sin = ang.sin().half().contiguous()
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self._keep = []
         lib = _abi.lib()
         model = _Model(batch, L, cfg.hidden, cfg.inter, cfg.q_heads, cfg.kv_heads, hd, max_tokens, cfg.rms_eps,
                        self.inv_freq.data_ptr(), self.final_norm.data_ptr(), self.hidden.data_ptr(),
-                       self.final_out.data_ptr(), 0)
+                       self.final_out.data_ptr(), 0, self.rope_cos.data_ptr(), self.rope_sin.data_ptr())
         self.act = torch.zeros(lib.tp_step_act_bytes(ctypes.addressof(model)), dtype=torch.uint8, device=dev)
         model.act = self.act.data_ptr()
         arr = (_Layer * L)()
@@ -139,9 +145,11 @@ class DecodeStep:
         _abi.check(lib.tp_step_build(ctypes.addressof(model), ctypes.addressof(arr), ctypes.addressof(self._image_host),
                                      nbytes, ctypes.addressof(ws)), "step_build")
         self._model, self._layers_c = model, arr
+        self.workspace = torch.zeros(int(ws.value), dtype=torch.uint8, device=dev)
+        _abi.check(lib.tp_step_bind(ctypes.addressof(self._image_host), self.workspace.data_ptr(),
+                                    self.workspace.numel()), "step_bind")
         host = torch.frombuffer(bytearray(self._image_host), dtype=torch.uint8)
         self.image = host.to(dev)
-        self.workspace = torch.zeros(int(ws.value), dtype=torch.uint8, device=dev)
         self.lm_head = GreedyLMHead(lm_head) if lm_head is not None else None
 
     # -- state ----------------------------------------------------------------
