@@ -90,7 +90,7 @@ struct alignas(16) LinearStage {
   int us, cps, rt_total, rpp, rs_smem, nin, pad2[2];
   // shared-memory offsets from the dynamic base: activations, input rows,
   // fp32 scratch, rotation scales, norm weight, producer scales
-  uint32_t z_off, xin_off, scr_off, rs_off, gam_off, psc_off, pad3[2];
+  uint32_t z_off, xin_off, scr_off, rs_off, gam_off, psc_off, stg_off, pad3;
   SliceSplit split[2];
   StepOp ops[kMaxStageOps];
 };
@@ -291,6 +291,12 @@ __device__ __forceinline__ void finish_chunk(const InVec& V, const ChunkRaw& r, 
   }
 }
 
+// Bytes per column and row of a stage's input staging area: fp16 base,
+// fp32 accumulator(s); a plain input is copied straight into xin.
+__host__ __device__ __forceinline__ int stage_bytes_per_col(int in_kind, int nin) {
+  return in_kind == kInSiluMul ? 8 : in_kind == kInRmsNorm ? 2 + 4 * nin : 0;
+}
+
 // Input transform of rows [b0, b0+rows) over slice columns [c0, c0+cols):
 // xin (fp16 bits, [rows][cols]) holds
 //   plain:    the input row;
@@ -299,91 +305,94 @@ __device__ __forceinline__ void finish_chunk(const InVec& V, const ChunkRaw& r, 
 //             with rinv[row] from here); h is also written back to L.hout,
 //             each CTA of the K-slice writing its share of the chunks;
 //   SiLU:     r16(r16(silu(gate)) * up).
-// Warps split over the rows (fixed order: deterministic sums); every lane
-// issues all its loads of a round before using them.
+// The dynamic inputs (base rows, accumulators: written by other SMs in
+// earlier stages) come into a shared-memory staging area with cp.async, all
+// copies in flight at once (one memory round trip, no registers held); the
+// transform then reads shared memory.  Warps split over the rows (fixed
+// order: deterministic sums).
 template <int KIND, bool ACC>
 __device__ __forceinline__ void stage_input_k(const LinearStage& L, int b0, int rows, int c0, int cols, uint16_t* xin,
-                                              float* red, const unsigned char* smem) {
+                                              float* red, unsigned char* smem) {
+  constexpr bool norm = KIND == kInRmsNorm, silu = KIND == kInSiluMul;
+  constexpr bool BASE = KIND != kInSiluMul;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* rinv = red + kStepMaxBatch * kStepWarps;
+  const int n8 = cols >> 3;
+  unsigned char* stg = smem + L.stg_off;
+  uint16_t* sb = KIND == kInPlain ? xin : reinterpret_cast<uint16_t*>(stg);
+  float* sa0 = reinterpret_cast<float*>(stg + (BASE ? rows * cols * 2 : 0));
+  float* sa1 = sa0 + rows * cols;
+  for (int i = tid; i < rows * n8; i += kStepThreads) {
+    const int r = i / n8, ci = i - r * n8, c = c0 + ci * 8;
+    const bool v = c < L.d;
+    const int64_t g = (int64_t)(b0 + r) * L.d + (v ? c : 0);
+    const int o = r * cols + ci * 8;
+    if constexpr (BASE) cp_async16(sb + o, L.in[0].base + g, v);
+    if constexpr (ACC) {
+      cp_async16(sa0 + o, L.in[0].acc + g, v);
+      cp_async16(sa0 + o + 4, L.in[0].acc + g + 4, v);
+    }
+    if constexpr (silu) {
+      cp_async16(sa1 + o, L.in[1].acc + g, v);
+      cp_async16(sa1 + o + 4, L.in[1].acc + g + 4, v);
+    }
+  }
+  cp_async_commit();
+  // the staging copies, the stage's static vectors (issued before its
+  // barrier) and the stage record in flight
+  cp_async_wait_all();
+  __syncthreads();
+  if constexpr (KIND == kInPlain) return;
   const int wpr = kStepWarps / rows, row = warp / wpr, sub = warp - row * wpr;
   const bool act = row < rows;
   const int64_t xrow = (int64_t)(b0 + (act ? row : 0)) * L.d;
-  // chunks per lane in flight (registers: 4 / 12 / 16 per chunk)
-  constexpr int U = KIND == kInPlain ? 4 : KIND == kInRmsNorm ? 3 : 2;
   const int stride = wpr * 32;
-  const int cpr = cols >> 3;
-  constexpr bool norm = KIND == kInRmsNorm, silu = KIND == kInSiluMul;
-  constexpr bool BASE = KIND != kInSiluMul;
   const uint16_t* psc = reinterpret_cast<const uint16_t*>(smem + L.psc_off);
   // CTAs of this K-slice share the write-back of h
   const int slice = blockIdx.x / L.cps, cta_in = blockIdx.x - slice * L.cps;
   float ssum = 0.f;
-  ChunkRaw r0[U], r1[silu ? U : 1];
-#define TP_STEP_ISSUE(CB)                                      \
-  _Pragma("unroll") for (int u = 0; u < U; ++u) {              \
-    const int ci = (CB) + u * stride, c = c0 + ci * 8;         \
-    if (ci < cpr && c < L.d) {                                 \
-      load_chunk<BASE, ACC>(L.in[0], xrow, c, r0[u]);          \
-      if constexpr (silu) load_chunk<false, true>(L.in[1], xrow, c, r1[u]); \
-    }                                                          \
-  }
-  const int cb0 = sub * 32 + lane;
-  if (act) {
-    TP_STEP_ISSUE(cb0)
-  }
-  // the stage's static vectors (cp.async group issued before its barrier;
-  // the newest group is a stage record still in flight)
-  cp_async_wait_group1();
-  __syncthreads();
-  for (int cb = cb0; act && cb < cpr; cb += stride * U) {
-    if (cb != cb0) {
-      TP_STEP_ISSUE(cb)
+  for (int ci = sub * 32 + lane; act && ci < n8; ci += stride) {
+    const int c = c0 + ci * 8, o = row * cols + ci * 8;
+    ChunkRaw r0, r1;
+    if constexpr (BASE) r0.base = *reinterpret_cast<const uint4*>(sb + o);
+    if constexpr (ACC) {
+      r0.a0 = *reinterpret_cast<const float4*>(sa0 + o);
+      r0.a1 = *reinterpret_cast<const float4*>(sa0 + o + 4);
     }
+    if constexpr (silu) {
+      r1.a0 = *reinterpret_cast<const float4*>(sa1 + o);
+      r1.a1 = *reinterpret_cast<const float4*>(sa1 + o + 4);
+    }
+    uint4 ov = make_uint4(0u, 0u, 0u, 0u);
+    if (c < L.d) {
+      float f[8];
+      finish_chunk<BASE, ACC>(L.in[0], r0, psc, ci * 8, c, f);
+      if constexpr (silu) {
+        float up[8];
+        finish_chunk<false, true>(L.in[1], r1, psc + cols, ci * 8, c, up);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int ci = cb + u * stride, c = c0 + ci * 8;
-      if (ci >= cpr) break;
-      uint4 o = make_uint4(0u, 0u, 0u, 0u);
-      if (c < L.d) {
-        float f[8];
-        finish_chunk<BASE, ACC>(L.in[0], r0[u], psc, ci * 8, c, f);
-        if constexpr (silu) {
-          float up[8];
-          finish_chunk<false, true>(L.in[1], r1[u], psc + cols, ci * 8, c, up);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = r16(r16(f[e] / (1.f + __expf(-f[e]))) * up[e]);
-        }
-        o = pack8(f);
-        if constexpr (norm) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
-          if (L.hout && ci % L.cps == cta_in) *reinterpret_cast<uint4*>(L.hout + xrow + c) = o;
-        }
+        for (int e = 0; e < 8; ++e) f[e] = r16(r16(f[e] / (1.f + __expf(-f[e]))) * up[e]);
       }
-      *reinterpret_cast<uint4*>(xin + row * cols + ci * 8) = o;
+      ov = pack8(f);
+      if constexpr (norm) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
+        if (L.hout && ci % L.cps == cta_in) *reinterpret_cast<uint4*>(L.hout + xrow + c) = ov;
+      }
     }
+    *reinterpret_cast<uint4*>(xin + row * cols + ci * 8) = ov;
   }
-#undef TP_STEP_ISSUE
   if constexpr (norm) {
     if (cols != L.d) {
       // K-split: the sum of squares needs the whole row (scales from global)
       ssum = 0.f;
-      const int dpr = L.d >> 3;
-      for (int cb = sub * 32 + lane; act && cb < dpr; cb += stride * U) {
-        ChunkRaw r0[U];
+      for (int cb = sub * 32 + lane; act && cb < (L.d >> 3); cb += stride) {
+        ChunkRaw r0;
+        load_chunk<BASE, ACC>(L.in[0], xrow, cb * 8, r0);
+        float f[8];
+        finish_chunk<BASE, ACC>(L.in[0], r0, L.in[0].scale, cb * 8, cb * 8, f);
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (cb + u * stride < dpr) load_chunk<BASE, ACC>(L.in[0], xrow, (cb + u * stride) * 8, r0[u]);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int c = (cb + u * stride) * 8;
-          if (c >= L.d) break;
-          float f[8];
-          finish_chunk<BASE, ACC>(L.in[0], r0[u], L.in[0].scale, c, c, f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
-        }
+        for (int e = 0; e < 8; ++e) ssum = fmaf(f[e], f[e], ssum);
       }
     }
     for (int o = 16; o; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
@@ -399,7 +408,7 @@ __device__ __forceinline__ void stage_input_k(const LinearStage& L, int b0, int 
 }
 
 __device__ __forceinline__ void stage_input(const LinearStage& L, int b0, int rows, int c0, int cols, uint16_t* xin,
-                                            float* red, const unsigned char* smem) {
+                                            float* red, unsigned char* smem) {
   if (L.in_kind == kInRmsNorm) {
     if (L.in[0].acc) stage_input_k<kInRmsNorm, true>(L, b0, rows, c0, cols, xin, red, smem);
     else stage_input_k<kInRmsNorm, false>(L, b0, rows, c0, cols, xin, red, smem);
@@ -564,7 +573,7 @@ __device__ void stage_static_prefetch(const LinearStage& L, unsigned char* smem)
 // Stage prologue: rotation scales to shared memory (async), the input
 // transform, every op's rotated activations, and the zero rows (CTAs of a
 // K-slice: the slice's columns).
-__device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
+__device__ __forceinline__ void stage_prologue(const LinearStage& L, unsigned char* smem, int B, float* red) {
   const int tid = threadIdx.x;
   const int slice = blockIdx.x / L.cps;
   if (slice >= L.kparts) return;
@@ -598,9 +607,39 @@ __device__ __noinline__ void stage_prologue(const LinearStage& L, unsigned char*
   __syncthreads();
 }
 
+// This warp's first weight unit of a linear stage and the trellis halo
+// before it (issued before the stage's barrier: the weights depend on
+// nothing it orders).
+__device__ __forceinline__ void preload_first(const LinearStage& L, uint4* pre, uint32_t& hg, uint32_t& hq) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  hg = hq = 0u;
+  const int slice = blockIdx.x / L.cps;
+  if (slice >= L.kparts) return;
+  const int wl = warp * L.cps + (blockIdx.x - slice * L.cps);
+  const SliceSplit& sp = L.split[slice == L.kparts - 1 ? 1 : 0];
+  if (wl >= sp.nw) return;
+  const int j0 = sp.start(wl);
+  if (j0 >= sp.start(wl + 1)) return;
+  const int rt = sp.row_tile(j0), ul = j0 - rt * sp.us;
+  int k = 0;
+  while (k + 1 < L.nops && rt >= L.ops[k + 1].rt_off) ++k;
+  const int64_t UB = 512 * L.bits;
+  const int us0 = slice * L.us;
+  const unsigned char* u = L.ops[k].stream + ((int64_t)(rt - L.ops[k].rt_off) * L.units_k + us0 + ul) * UB;
+  const uint4* src = reinterpret_cast<const uint4*>(u) + lane * L.bits;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (q < L.bits) pre[q] = ldg_stream(src + q);
+  if (us0 + ul > 0) {
+    const uint4 pv = ldg_stream(reinterpret_cast<const uint4*>(u - UB) + lane * L.bits);
+    hg = pv.z;
+    hq = pv.w;
+  }
+}
+
 template <int BITS>
-__device__ __noinline__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
-                                             int sidx) {
+__device__ __forceinline__ void linear_stage(const LinearStage& L, unsigned char* smem, int B, const unsigned char* lut,
+                                             int sidx, const uint4* pre, uint32_t pre_hg, uint32_t pre_hq) {
   constexpr int S = 64;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -628,22 +667,14 @@ __device__ __noinline__ void linear_stage(const LinearStage& L, unsigned char* s
   const int zst = L.us * kUnitCols + kZPad;
   __half* z = reinterpret_cast<__half*>(smem + L.z_off);
 
-  // ---- first unit of the run and its trellis halo (in L2: prefetched
-  // before the barrier) ----
+  // ---- first unit of the run and its trellis halo: loaded by
+  // preload_first before the barrier that preceded the stage ----
   int rt = sp.row_tile(j0), ul = j0 - rt * Us;
   int opk = op_of(rt);
   uint4 wa[BITS];
-  uint32_t hg = 0u, hq = 0u, hng = 0u, hnq = 0u;
-  if (j0 < j1) {
-    const uint4* src = reinterpret_cast<const uint4*>(unit_ptr(opk, rt, ul)) + lane * BITS;
 #pragma unroll
-    for (int k = 0; k < BITS; ++k) wa[k] = ldg_stream(src + k);
-    if (us0 + ul > 0) {
-      const uint4 pv = ldg_stream(reinterpret_cast<const uint4*>(unit_ptr(opk, rt, ul - 1)) + lane * BITS);
-      hg = pv.z;
-      hq = pv.w;
-    }
-  }
+  for (int k = 0; k < BITS; ++k) wa[k] = pre[k];
+  uint32_t hg = pre_hg, hq = pre_hq, hng = 0u, hnq = 0u;
   step_trace(sidx, 1);
 
   // ---- decode + MMA over the run ----
@@ -870,17 +901,15 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   const int64_t kv0 = ((int64_t)b * A.kv_heads + kvh) * A.max_t;
   // this warp's first cached tokens, loaded before anything waits
   HRaw<E> kr[kTok], vr[kTok];
-  auto load_tokens = [&](int first) {
-#pragma unroll
-    for (int i = 0; i < kTok; ++i) {
-      const int tk = first + i * kStepWarps;
-      if (tk < t1 && tk != pos) {
-        kr[i] = ld_hraw<E>(A.k_cache + (kv0 + tk) * hd + lane * E);
-        vr[i] = ld_hraw<E>(A.v_cache + (kv0 + tk) * hd + lane * E);
-      }
-    }
-  };
-  load_tokens(t0 + warp);
+#define TP_ATTN_LOAD(K, V, FIRST)                                \
+  _Pragma("unroll") for (int i = 0; i < kTok; ++i) {             \
+    const int tk = (FIRST) + i * kStepWarps;                     \
+    if (tk < t1 && tk != pos) {                                  \
+      K[i] = ld_hraw<E>(A.k_cache + (kv0 + tk) * hd + lane * E); \
+      V[i] = ld_hraw<E>(A.v_cache + (kv0 + tk) * hd + lane * E); \
+    }                                                            \
+  }
+  TP_ATTN_LOAD(kr, vr, t0 + warp)
   // q heads of the group (one warp per head) and the new token's k / v
   const bool newtok = t1 == T && t0 < t1;
   if (warp < gs || (warp == kStepWarps - 1 && newtok)) {
@@ -946,23 +975,21 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
     for (int e = 0; e < E; ++e) acc[j][e] = 0.f;
   }
   for (int first = t0 + warp; first < t1; first += kTok * kStepWarps) {
-    float kx[kTok][E], vx[kTok][E];
+    // the next tokens load while these are used
+    HRaw<E> kn[kTok], vn[kTok];
+    TP_ATTN_LOAD(kn, vn, first + kTok * kStepWarps)
 #pragma unroll
     for (int i = 0; i < kTok; ++i) {
       const int tk = first + i * kStepWarps;
+      if (tk >= t1) break;
+      float kx[E], vx[E];
       if (tk == pos) {
 #pragma unroll
-        for (int e = 0; e < E; ++e) kx[i][e] = knew[lane * E + e], vx[i][e] = vnew[lane * E + e];
+        for (int e = 0; e < E; ++e) kx[e] = knew[lane * E + e], vx[e] = vnew[lane * E + e];
       } else {
-        cvt_hraw<E>(kr[i], kx[i]);
-        cvt_hraw<E>(vr[i], vx[i]);
+        cvt_hraw<E>(kr[i], kx);
+        cvt_hraw<E>(vr[i], vx);
       }
-    }
-    // the next tokens load while these are used
-    load_tokens(first + kTok * kStepWarps);
-#pragma unroll
-    for (int i = 0; i < kTok; ++i) {
-      if (first + i * kStepWarps >= t1) break;
 #pragma unroll
       for (int j = 0; j < G; ++j) {
         if (j >= gs) break;
@@ -976,7 +1003,7 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
         }
         float sc = 0.f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) sc = fmaf(qv[e], kx[i][e], sc);
+        for (int e = 0; e < E; ++e) sc = fmaf(qv[e], kx[e], sc);
         for (int o = 16; o; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
         // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
         sc = r16(r16(sc) * A.scaling);
@@ -984,11 +1011,14 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
         const float corr = __expf(m[j] - mn), p = __expf(sc - mn);
         l[j] = l[j] * corr + p;
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[i][e]);
+        for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[e]);
         m[j] = mn;
       }
     }
+#pragma unroll
+    for (int i = 0; i < kTok; ++i) kr[i] = kn[i], vr[i] = vn[i];
   }
+#undef TP_ATTN_LOAD
   step_mark(5);
   // combine the warps
   const int ws_ = hd + 2;
@@ -1034,45 +1064,30 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   const int wph = kStepWarps / gs, j = warp % gs, quarter = warp / gs;
   const int per = hd / wph;  // columns per warp: 8 .. 64
   const int dd0 = quarter * per;
-  constexpr int kC = 16;  // splits per pass
-  float M = -INFINITY;
   float ms = -INFINITY, ls = 0.f;
   if (lane < A.nsplit) {
     ms = __ldcg(gp + (lane * gs + j) * ws_);
     ls = __ldcg(gp + (lane * gs + j) * ws_ + 1);
   }
-  float av[kC][2];
-  auto load_av = [&](int s0) {
+  // every split's value of this lane's column (dd0 + h + lane) in flight
+  // together with the split maxima and sums: one memory round trip per 32
+  // columns of the warp
+  for (int h = 0; h < per; h += 32) {
+    const bool on = lane + h < per;
+    float av[kMaxSplits];
 #pragma unroll
-    for (int s2 = 0; s2 < kC; ++s2) {
-      if (s0 + s2 < A.nsplit) {
-        const float* src = gp + ((s0 + s2) * gs + j) * ws_ + 2 + dd0;
-        av[s2][0] = lane < per ? __ldcg(src + lane) : 0.f;
-        av[s2][1] = lane + 32 < per ? __ldcg(src + lane + 32) : 0.f;
-      }
-    }
-  };
-  load_av(0);
-  M = ms;
-  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float fs = ms == -INFINITY ? 0.f : __expf(ms - M);
-  float Lsum = fs * ls;
-  for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-  float o0 = 0.f, o1 = 0.f;
-  for (int s0 = 0; s0 < A.nsplit; s0 += kC) {
-    if (s0 > 0) load_av(s0);
+    for (int s2 = 0; s2 < kMaxSplits; ++s2)
+      av[s2] = s2 < A.nsplit && on ? __ldcg(gp + (s2 * gs + j) * ws_ + 2 + dd0 + h + lane) : 0.f;
+    float M = ms;
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float fs = ms == -INFINITY ? 0.f : __expf(ms - M);
+    float Lsum = fs * ls;
+    for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+    float ao = 0.f;
 #pragma unroll
-    for (int s2 = 0; s2 < kC; ++s2) {
-      const float f = __shfl_sync(0xffffffffu, fs, (s0 + s2) & 31);
-      if (s0 + s2 < A.nsplit) {
-        o0 = fmaf(f, av[s2][0], o0);
-        o1 = fmaf(f, av[s2][1], o1);
-      }
-    }
+    for (int s2 = 0; s2 < kMaxSplits; ++s2) ao = fmaf(__shfl_sync(0xffffffffu, fs, s2), av[s2], ao);
+    if (on) A.out[(int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd0 + h + lane] = f2h(ao / Lsum);
   }
-  uint16_t* dst = A.out + (int64_t)b * A.q_heads * hd + (kvh * gs + j) * hd + dd0;
-  if (lane < per) dst[lane] = f2h(o0 / Lsum);
-  if (lane + 32 < per) dst[lane + 32] = f2h(o1 / Lsum);
   step_mark(7);
   if (tid == 0) counters[cgroup] = 0u;
 }
@@ -1215,7 +1230,12 @@ __global__ void __launch_bounds__(kStepThreads, 1)
   fetch(1);
   cp_async_wait_all();
   __syncthreads();
-  if (H.nstages > 0 && slots[0].type == kLinear) stage_static_prefetch(slots[0].lin, smem);
+  uint4 pre[4];
+  uint32_t pre_hg = 0u, pre_hq = 0u;
+  if (H.nstages > 0 && slots[0].type == kLinear) {
+    stage_static_prefetch(slots[0].lin, smem);
+    preload_first(slots[0].lin, pre, pre_hg, pre_hq);
+  }
   for (int s = 0; s < H.nstages; ++s) {
     const StepStage& st = slots[s % 3];
     fetch(s + 2);
@@ -1237,9 +1257,9 @@ __global__ void __launch_bounds__(kStepThreads, 1)
       }
       stage_prologue(L, smem, H.B, red);
       step_trace(s, 1);
-      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, s);
-      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, s);
-      else linear_stage<4>(L, smem, H.B, lut4, s);
+      if (L.bits == 2) linear_stage<2>(L, smem, H.B, lut3, s, pre, pre_hg, pre_hq);
+      else if (L.bits == 3) linear_stage<3>(L, smem, H.B, lut3, s, pre, pre_hg, pre_hq);
+      else linear_stage<4>(L, smem, H.B, lut4, s, pre, pre_hg, pre_hq);
     } else if (st.type == kAttention) {
       attn_stage(st.attn, H.B, pos, smem, ws, H);
     } else {
@@ -1253,6 +1273,7 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     if (nx.type == kLinear) {
       prefetch_stage(nx.lin);
       stage_static_prefetch(nx.lin, smem);
+      preload_first(nx.lin, pre, pre_hg, pre_hq);
     }
     if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x + (unsigned)H.extra_arrivals, limit_ns, s_ok)) break;
     step_trace(s, 3);
@@ -1294,8 +1315,9 @@ void linear_sizes(const LinearStage& L, int B, int cols, int rpp, int rs_smem, u
   sz[3] = r128((int64_t)rs_smem * L.nops * cols * 2);
   sz[4] = L.in_kind == kInRmsNorm ? r128((int64_t)cols * 2) : 0u;
   sz[5] = r128((int64_t)L.nin * cols * 2);
+  sz[6] = r128((int64_t)rpp * cols * stage_bytes_per_col(L.in_kind, L.nin));
 }
-constexpr int kBufs = 6;
+constexpr int kBufs = 7;
 
 // Plan one linear stage (ops share d, block, bits, codebook); the input
 // description (in_kind, in[], nin) is set by the caller before.
@@ -1338,7 +1360,7 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
   // first -- a small shared-memory footprint leaves the SM more L1 -- then
   // to region b (after the table).
   int us = 0, kparts = 0, rpp = 0, rs_smem = 1;
-  uint32_t off[kBufs] = {0, 0, 0, 0, 0, 0};
+  uint32_t off[kBufs] = {0, 0, 0, 0, 0, 0, 0};
   bool found = false;
   auto place = [&](const uint32_t* sz) {
     uint32_t ua = 0, ub = 0;
@@ -1360,9 +1382,17 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
     }
     return true;
   };
+  // Stages whose input is not normed split K so that each CTA reads and
+  // rotates at most kSliceTarget units of columns: their K-slices add into
+  // the same accumulators, so a split costs nothing downstream.  A norm needs
+  // the whole row in every CTA, so those start from one slice.
+  constexpr int kSliceTarget = 10;
+  const int kp0 = L.in_kind == kInRmsNorm
+                      ? 1
+                      : std::max(1, std::min((U + kSliceTarget - 1) / kSliceTarget, (U + blk_units - 1) / blk_units));
   for (int attempt = 0; attempt < 2 && !found; ++attempt) {
     rs_smem = attempt == 0 ? 1 : 0;
-    for (kparts = 1; kparts <= U && !found; ++kparts) {
+    for (kparts = kp0; kparts <= U && !found; ++kparts) {
       us = (U + kparts - 1) / kparts;
       us = (us + blk_units - 1) / blk_units * blk_units;
       const int kp = (U + us - 1) / us;
@@ -1390,6 +1420,7 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
   L.rs_off = off[3];
   L.gam_off = off[4];
   L.psc_off = off[5];
+  L.stg_off = off[6];
   // grid split
   L.cps = std::max(1, G / kparts);
   const int64_t W = (int64_t)L.cps * kStepWarps;
@@ -1663,7 +1694,7 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
     const LinearStage& L = st[s].lin;
     uint32_t sz[kBufs];
     linear_sizes(L, B, L.us * kUnitCols, L.rpp, L.rs_smem, sz);
-    const uint32_t offs[kBufs] = {L.z_off, L.xin_off, L.scr_off, L.rs_off, L.gam_off, L.psc_off};
+    const uint32_t offs[kBufs] = {L.z_off, L.xin_off, L.scr_off, L.rs_off, L.gam_off, L.psc_off, L.stg_off};
     for (int i = 0; i < kBufs; ++i)
       if (sz[i]) end = std::max(end, R.base + offs[i] + sz[i]);
   }
