@@ -61,7 +61,9 @@ def test_step_barrier_timeout_is_reported_and_context_recovers():
     out = step.run()
     step.status()
     torch.cuda.synchronize()
-    assert torch.equal(out, ref)
+    # the linears' partial sums meet in fp32 atomics (summation order varies
+    # between runs), so the comparison allows a few fp16 ulps
+    assert float((out.float() - ref.float()).norm() / ref.float().norm()) < 2e-3
 
 
 def test_gemv_status_reports_and_clears_counter_block():
