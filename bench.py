@@ -275,11 +275,18 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
     bits, B = args.bits, args.batch
     mods = build_model(cfg, bits, dev, seed=args.seed)  # identical on every rank
     step_bytes = sum(gemv_bytes(n, d, bits, B) for _ in range(cfg["layers"]) for _, d, n in linear_shapes(cfg))
+    x_host = torch.randn(B, cfg["hidden"], dtype=torch.float16, generator=torch.Generator().manual_seed(5)).pin_memory()
+    # parity reference: the same model as a single-GPU engine on this rank
+    from turbopress_b200.engine import DecodeEngine
+
+    ref_eng = DecodeEngine(mods, engine_inputs(cfg["layers"]), batch=B, input_dtype=torch.float16)
+    ref_out = [o.clone() for o in ref_eng.run(x_host.to(dev))]
+    ref_eng.check()
+    del ref_eng
     eng = TPDecodeEngine(mods, engine_inputs(cfg["layers"]), batch=B, input_dtype=torch.float16)
     del mods
     torch.cuda.empty_cache()
     stream = torch.cuda.Stream(device=dev)
-    x_host = torch.randn(B, cfg["hidden"], dtype=torch.float16).pin_memory()
     y_host = torch.empty(B, cfg["hidden"], dtype=torch.float32).pin_memory()
     xin = eng.x_ext[cfg["hidden"]]
 
@@ -293,6 +300,9 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
             eng.launch()
         stream.synchronize()
         eng.check()
+        # every op's full output on this rank against the single-GPU engine
+        parity = max(float((o - r).norm() / r.norm().clamp_min(1e-30)) for o, r in zip(eng.outputs, ref_out))
+        del ref_out
         # graphs of two consecutive runs (the arena alternates per run)
         if eng.step % 2:
             eng.launch()
@@ -342,9 +352,9 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
         e1.synchronize()
         ms_e2e = e0.elapsed_time(e1) / steps
         eng.check()
-    t = torch.tensor([ms, ms_e2e, ms_kernel], device=dev)
+    t = torch.tensor([ms, ms_e2e, ms_kernel, parity], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e, ms_kernel = (float(v) for v in t)
+    ms, ms_e2e, ms_kernel, parity = (float(v) for v in t)
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -374,6 +384,11 @@ def run_tp(args, cfg, rank, world, local, dev, dist) -> dict | None:
                    "l2": "inputs larger than L2 (packed weights per GPU per step > 126 MB L2)",
                    "parallelism": f"tp{world}"},
         "tok_s": round(B * 1000.0 / ms, 1),
+        # worst relative L2 over every op's full output on every rank against a
+        # single-GPU engine run of the same model (checked before timing); the
+        # ops are chained (each output, rounded to fp16, is a later op's input),
+        # so fp32 summation-order differences compound along the 252 ops
+        "tp_parity_rel_l2": float(f"{parity:.3e}"),
         "e2e": {"value": round(step_bytes / (ms_e2e * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "tok_s": round(B * 1000.0 / ms_e2e, 1),
                 "h2d_bytes_per_step": int(x_host.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 4)},
@@ -614,7 +629,8 @@ def run_decode(args) -> dict | None:
         out["tp"] = {"parallelism": f"tp{world}", "ms_per_step": tp_line["ms_per_step"], "tok_s": tp_line["tok_s"],
                      "value": tp_line["value"], "unit": "GB/s", "e2e_tok_s": tp_line["e2e"]["tok_s"],
                      "kernel_ms": tp_line["roofline"]["kernel_ms"], "roofline_frac": tp_line["roofline"]["frac"],
-                     "path": tp_line["config"]["path"], "workload": "decoder linears only (no attention)"}
+                     "path": tp_line["config"]["path"], "workload": "decoder linears only (no attention)",
+                     "tp_parity_rel_l2": tp_line["tp_parity_rel_l2"]}
     if world == 1 and not args.quick:
         out["gemv_c3"] = gemv_table(args, dev)
         out["c1"] = c1_section(args, dev)
