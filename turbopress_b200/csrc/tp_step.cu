@@ -891,7 +891,8 @@ template <int E, int G>
 __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int sp, int pos, unsigned char* buf,
                                           float* part, unsigned* counters, int cgroup, unsigned* s_last) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hd = A.hd, gs = A.q_heads / A.kv_heads;
+  const int hd = A.hd, gs = G;  // G: the exact query heads per kv head
+  constexpr int kT = G >= 8 ? 2 : kTok;  // cached tokens per warp in flight
   float* sq = reinterpret_cast<float*>(buf);                 // [gs][hd] normed, roped q
   float* knew = sq + kMaxGroup * hd;                         // [hd]
   float* vnew = knew + hd;                                   // [hd]
@@ -900,9 +901,9 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
   const int t0 = sp * Ls, t1 = min(T, t0 + Ls);
   const int64_t kv0 = ((int64_t)b * A.kv_heads + kvh) * A.max_t;
   // this warp's first cached tokens, loaded before anything waits
-  HRaw<E> kr[kTok], vr[kTok];
+  HRaw<E> kr[kT], vr[kT];
 #define TP_ATTN_LOAD(K, V, FIRST)                                \
-  _Pragma("unroll") for (int i = 0; i < kTok; ++i) {             \
+  _Pragma("unroll") for (int i = 0; i < kT; ++i) {             \
     const int tk = (FIRST) + i * kStepWarps;                     \
     if (tk < t1 && tk != pos) {                                  \
       K[i] = ld_hraw<E>(A.k_cache + (kv0 + tk) * hd + lane * E); \
@@ -974,49 +975,79 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[j][e] = 0.f;
   }
-  for (int first = t0 + warp; first < t1; first += kTok * kStepWarps) {
+  for (int first = t0 + warp; first < t1; first += kT * kStepWarps) {
     // the next tokens load while these are used
-    HRaw<E> kn[kTok], vn[kTok];
-    TP_ATTN_LOAD(kn, vn, first + kTok * kStepWarps)
+    HRaw<E> kn[kT], vn[kT];
+    TP_ATTN_LOAD(kn, vn, first + kT * kStepWarps)
+    // the chunk's tokens (past t1: masked) -- every (token, head) score
+    // reduced together, then one online-softmax rescale per head
+    float kx[kT][E], vx[kT][E];
+    bool valid[kT];
 #pragma unroll
-    for (int i = 0; i < kTok; ++i) {
+    for (int i = 0; i < kT; ++i) {
       const int tk = first + i * kStepWarps;
-      if (tk >= t1) break;
-      float kx[E], vx[E];
-      if (tk == pos) {
+      valid[i] = tk < t1;
+      if (!valid[i]) {  // masked below; its registers hold no loaded data
 #pragma unroll
-        for (int e = 0; e < E; ++e) kx[e] = knew[lane * E + e], vx[e] = vnew[lane * E + e];
+        for (int e = 0; e < E; ++e) kx[i][e] = vx[i][e] = 0.f;
+      } else if (tk == pos) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) kx[i][e] = knew[lane * E + e], vx[i][e] = vnew[lane * E + e];
       } else {
-        cvt_hraw<E>(kr[i], kx);
-        cvt_hraw<E>(vr[i], vx);
+        cvt_hraw<E>(kr[i], kx[i]);
+        cvt_hraw<E>(vr[i], vx[i]);
+      }
+    }
+    float sc[kT][G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      float qv[E];
+      if constexpr (E == 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(sq + j * hd + lane * 4);
+        qv[0] = q4.x, qv[1] = q4.y, qv[2] = q4.z, qv[3] = q4.w;
+      } else {
+        const float2 q2 = *reinterpret_cast<const float2*>(sq + j * hd + lane * 2);
+        qv[0] = q2.x, qv[1] = q2.y;
       }
 #pragma unroll
-      for (int j = 0; j < G; ++j) {
-        if (j >= gs) break;
-        float qv[E];
-        if constexpr (E == 4) {
-          const float4 q4 = *reinterpret_cast<const float4*>(sq + j * hd + lane * 4);
-          qv[0] = q4.x, qv[1] = q4.y, qv[2] = q4.z, qv[3] = q4.w;
-        } else {
-          const float2 q2 = *reinterpret_cast<const float2*>(sq + j * hd + lane * 2);
-          qv[0] = q2.x, qv[1] = q2.y;
-        }
-        float sc = 0.f;
+      for (int i = 0; i < kT; ++i) {
+        float d = 0.f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) sc = fmaf(qv[e], kx[e], sc);
-        for (int o = 16; o; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-        // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
-        sc = r16(r16(sc) * A.scaling);
-        const float mn = fmaxf(m[j], sc);
-        const float corr = __expf(m[j] - mn), p = __expf(sc - mn);
-        l[j] = l[j] * corr + p;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[j][e] = fmaf(acc[j][e], corr, p * vx[e]);
-        m[j] = mn;
+        for (int e = 0; e < E; ++e) d = fmaf(qv[e], kx[i][e], d);
+        sc[i][j] = d;
       }
     }
 #pragma unroll
-    for (int i = 0; i < kTok; ++i) kr[i] = kn[i], vr[i] = vn[i];
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < kT; ++i)
+#pragma unroll
+        for (int j = 0; j < G; ++j) sc[i][j] += __shfl_xor_sync(0xffffffffu, sc[i][j], o);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      // the reference's fp16 scores: fp16(q.k), then fp16(* scaling)
+      float mx = m[j];
+#pragma unroll
+      for (int i = 0; i < kT; ++i) {
+        sc[i][j] = valid[i] ? r16(r16(sc[i][j]) * A.scaling) : -INFINITY;
+        mx = fmaxf(mx, sc[i][j]);
+      }
+      const float corr = m[j] == -INFINITY ? 0.f : __expf(m[j] - mx);
+      float lsum = l[j] * corr;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[j][e] *= corr;
+#pragma unroll
+      for (int i = 0; i < kT; ++i) {
+        const float p = valid[i] ? __expf(sc[i][j] - mx) : 0.f;
+        lsum += p;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[j][e] = fmaf(p, vx[i][e], acc[j][e]);
+      }
+      l[j] = lsum;
+      m[j] = mx;
+    }
+#pragma unroll
+    for (int i = 0; i < kT; ++i) kr[i] = kn[i], vr[i] = vn[i];
   }
 #undef TP_ATTN_LOAD
   step_mark(5);
@@ -1103,13 +1134,19 @@ __device__ void attn_stage(const AttnStage& A, int B, int pos, unsigned char* sm
     const int grp = it / A.nsplit, sp = it - grp * A.nsplit;
     const int b = grp / A.kv_heads, kvh = grp - b * A.kv_heads;
     const int gs = A.q_heads / A.kv_heads;
+#define TP_ATTN_CALL(E_)                                                                        \
+  switch (gs) {                                                                                 \
+    case 1: attn_item<E_, 1>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last); break;       \
+    case 2: attn_item<E_, 2>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last); break;       \
+    case 4: attn_item<E_, 4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last); break;       \
+    default: attn_item<E_, 8>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last); break;      \
+  }
     if (A.hd == 128) {
-      if (gs <= 4) attn_item<4, 4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
-      else attn_item<4, kMaxGroup>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+      TP_ATTN_CALL(4)
     } else {
-      if (gs <= 4) attn_item<2, 4>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
-      else attn_item<2, kMaxGroup>(A, b, kvh, sp, pos, buf, part, counters, grp, s_last);
+      TP_ATTN_CALL(2)
     }
+#undef TP_ATTN_CALL
     __syncthreads();
   }
 }
