@@ -1397,6 +1397,7 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
   // first -- a small shared-memory footprint leaves the SM more L1 -- then
   // to region b (after the table).
   int us = 0, kparts = 0, rpp = 0, rs_smem = 1;
+  bool alias = false;
   uint32_t off[kBufs] = {0, 0, 0, 0, 0, 0, 0};
   bool found = false;
   auto place = [&](const uint32_t* sz) {
@@ -1438,6 +1439,13 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
       for (rpp = B; rpp >= 1; --rpp) {
         uint32_t sz[kBufs];
         linear_sizes(L, B, cols, rpp, rs_smem, sz);
+        // the producer scales and the input staging are dead before the
+        // rotation writes the activations: they share the activations'
+        // buffer when they fit in it (a smaller footprint leaves more L1)
+        // (one pass over the batch rows only: a second pass would stage
+        // over the first pass's activations)
+        alias = rpp == B && sz[5] + sz[6] <= sz[0];
+        if (alias) sz[5] = sz[6] = 0;
         if (place(sz)) {
           found = true;
           break;
@@ -1458,6 +1466,12 @@ tp_status plan_linear(LinearStage& L, const tp_step_linear* const* ops, float* c
   L.gam_off = off[4];
   L.psc_off = off[5];
   L.stg_off = off[6];
+  if (alias) {
+    uint32_t sz[kBufs];
+    linear_sizes(L, B, us * kUnitCols, rpp, rs_smem, sz);
+    L.psc_off = L.z_off;
+    L.stg_off = L.z_off + sz[5];
+  }
   // grid split
   L.cps = std::max(1, G / kparts);
   const int64_t W = (int64_t)L.cps * kStepWarps;
@@ -1718,13 +1732,13 @@ extern "C" tp_status tp_step_build(const tp_step_model* m, const tp_step_layer* 
     s.fnorm.hout = m->hidden_state;
     s.fnorm.d = m->hidden;
     s.fnorm.eps = m->rms_eps;
-    s.fnorm.buf_off = R.b0 - R.base;
+    s.fnorm.buf_off = (!has4 && R.a0 + hid * 2 <= R.a1 ? R.a0 : R.b0) - R.base;
     zero(s, acc_g, inter), zero(s, acc_u, inter);  // read by the last DOWN; acc_d: cleared by the stage itself
   }
   if (zero_overflow) return fail(TP_ERR_UNSUPPORTED, "tp_step: internal error (zero list)");
   // the largest footprint over the stages sets the dynamic shared memory size
   uint32_t end = std::max<uint32_t>(has4 ? R.b0 : kLutAbs + 65536u, attn_at + attn_buf);
-  end = std::max<uint32_t>(end, R.b0 + static_cast<uint32_t>(hid * 2));
+  end = std::max<uint32_t>(end, R.base + st[ns - 1].fnorm.buf_off + static_cast<uint32_t>(hid * 2));
   if (R.b0 + hid * 2 > R.b1) return fail(TP_ERR_UNSUPPORTED, "tp_step: hidden size too large");
   for (int s = 0; s < ns; ++s) {
     if (st[s].type != kLinear) continue;
