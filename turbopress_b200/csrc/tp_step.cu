@@ -196,12 +196,18 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // (after a release fence) and spins on acquire loads until `target`; bounded
 // by kBarrierNs of global time, after which it sets the status and every
 // CTA abandons the step.
-__device__ bool grid_barrier(unsigned* bar, unsigned* status, unsigned target, unsigned long long limit_ns,
-                             int* s_ok) {
+// Arrival: after a CTA barrier (every thread's writes of the stage are
+// done), thread 0 adds one with release semantics at GPU scope (a reduction:
+// it does not wait for the add to complete, so the CTA goes on with work that
+// does not depend on the barrier).
+__device__ __forceinline__ void grid_arrive(unsigned* bar) {
   __syncthreads();
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+// Wait: thread 0 spins on acquire loads until the counter reaches `target`.
+__device__ bool grid_wait(unsigned* bar, unsigned* status, unsigned target, unsigned long long limit_ns, int* s_ok) {
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
     int ok = 0;
     const unsigned long long t0 = global_ns();
     for (unsigned i = 0;; ++i) {
@@ -1304,15 +1310,17 @@ __global__ void __launch_bounds__(kStepThreads, 1)
     }
     step_trace(s, 2);
     if (s + 1 == H.nstages) break;
+    grid_arrive(bar);     // this stage's results are published
     cp_async_wait_all();  // the next records have landed
     __syncthreads();      // and this stage's shared buffers are free
+    // work that depends on nothing the barrier orders, while it completes
     const StepStage& nx = slots[(s + 1) % 3];
     if (nx.type == kLinear) {
       prefetch_stage(nx.lin);
       stage_static_prefetch(nx.lin, smem);
       preload_first(nx.lin, pre, pre_hg, pre_hq);
     }
-    if (!grid_barrier(bar, status, (unsigned)(s + 1) * gridDim.x + (unsigned)H.extra_arrivals, limit_ns, s_ok)) break;
+    if (!grid_wait(bar, status, (unsigned)(s + 1) * gridDim.x + (unsigned)H.extra_arrivals, limit_ns, s_ok)) break;
     step_trace(s, 3);
   }
 }
