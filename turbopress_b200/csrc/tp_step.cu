@@ -1086,14 +1086,19 @@ __device__ __noinline__ void attn_item(const AttnStage& A, int b, int kvh, int s
       __stcg(mypart + j * ws_ + 1, Lsum);
     }
   }
-  // the last CTA of the (b, kvh) group combines the splits
-  __threadfence();
+  // the last CTA of the (b, kvh) group combines the splits: one acq_rel
+  // add by thread 0 after the CTA barrier publishes this split's partials
+  // (release, cumulative over the CTA's writes) and, for the last split,
+  // orders its reads of the others' partials (acquire)
   __syncthreads();
-  if (tid == 0) *s_last = atomicAdd(&counters[cgroup], 1u) == (unsigned)(A.nsplit - 1) ? 1u : 0u;
+  if (tid == 0) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&counters[cgroup]) : "memory");
+    *s_last = old == (unsigned)(A.nsplit - 1) ? 1u : 0u;
+  }
   __syncthreads();
   step_mark(6);
   if (!*s_last) return;
-  __threadfence();
   // warp w: head j = w % gs, a 1 / (16 / gs) share of its columns; lane s
   // holds split s's max and sum, every lane its columns of all splits (all
   // loads in flight at once)
