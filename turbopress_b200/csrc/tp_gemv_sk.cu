@@ -334,17 +334,23 @@ __global__ void __launch_bounds__(kSkThreads, 1) tcq_gemv_sk_kernel(SkParams p) 
         const int col = 2 * t + (e & 1), row = g + 8 * (e >> 1);
         if (col < B) __stcg(pc + row * B + col, v[e]);
       }
-      __threadfence();
       __syncwarp();
       const SliceSplit& s0 = p.split[0];
       const SliceSplit& s1 = p.split[1];
       const int c0 = s0.warp_of((frt + 1) * s0.us - 1) - s0.warp_of(frt * s0.us) + 1;
       const int c1 = s1.warp_of((frt + 1) * s1.us - 1) - s1.warp_of(frt * s1.us) + 1;
+      // one acq_rel add by lane 0 after the warp barrier: publishes the
+      // warp's partials (release, cumulative over the warp's stores) and, for
+      // the last warp of the tile, orders its reads of the others' (acquire)
       unsigned last = 0u;
-      if (lane == 0) last = atomicAdd(&p.counters[frt], 1u) == (unsigned)((p.kparts - 1) * c0 + c1 - 1) ? 1u : 0u;
+      if (lane == 0) {
+        unsigned old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&p.counters[frt]) : "memory");
+        last = old == (unsigned)((p.kparts - 1) * c0 + c1 - 1) ? 1u : 0u;
+      }
       last = __shfl_sync(0xffffffffu, last, 0);
       if (!last) return;
-      __threadfence();
+      __syncwarp();
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = 0.f;
       for (int sl = 0; sl < p.kparts; ++sl) {
