@@ -68,11 +68,11 @@ LINEARS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down
 # DRAM bytes (read + write) of one engine launch / algorithmic bytes of the
 # step, from the ncu capture summarised under profiles/ (None: not captured)
 TRAFFIC_RATIO = 1.025
-# DRAM bytes (read 185.03 MB + write 4.93 MB) of one step_kernel launch over
+# DRAM bytes (read 185.44 MB + write 4.13 MB) of one step_kernel launch over
 # the first 4 layers of the Qwen3-4B 3-bit batch-1 line / its algorithmic
 # bytes (169.12 MB); the traffic of every layer is the same, so the ratio
 # scales to the full step (profiles/step_kernel_qwen3-4b_4layer_3bit_b1.md)
-STEP_TRAFFIC = {("qwen3-4b", 3, 1): (185_026_560 + 4_928_000) / 169_115_520}
+STEP_TRAFFIC = {("qwen3-4b", 3, 1): (185_441_024 + 4_134_912) / 169_115_520}
 
 
 def linear_shapes(cfg: dict) -> list[tuple[str, int, int]]:
