@@ -206,3 +206,26 @@ def test_step_greedy_tokens_match_hf():
     # every mismatch above was a near-tie; the fp32 atomics' summation order
     # decides a few of those differently from run to run
     assert agree >= 28, (agree, near)
+
+
+def test_step_bind_and_run_argument_checks():
+    """tp_step_run refuses an image bound to another workspace, and
+    tp_step_bind refuses to rebind it."""
+    import ctypes
+
+    from turbopress_b200 import _abi
+
+    step = _build(_small_cfg(), [3, 3], 1)
+    lib = _abi.lib()
+    other = torch.zeros_like(step.workspace)
+    st = torch.cuda.current_stream().cuda_stream
+    rc = lib.tp_step_run(step.image.data_ptr(), ctypes.addressof(step._image_host), step.pos.data_ptr(),
+                         other.data_ptr(), other.numel(), st)
+    assert rc == _abi.TP_ERR_ARG and b"not bound" in lib.tp_last_error()
+    rc = lib.tp_step_bind(ctypes.addressof(step._image_host), other.data_ptr(), other.numel())
+    assert rc == _abi.TP_ERR_ARG
+    assert lib.tp_step_bind(ctypes.addressof(step._image_host), step.workspace.data_ptr(),
+                            step.workspace.numel()) == _abi.TP_OK
+    small = torch.zeros(256, dtype=torch.uint8, device=DEV)
+    assert lib.tp_step_run(step.image.data_ptr(), ctypes.addressof(step._image_host), step.pos.data_ptr(),
+                           small.data_ptr(), small.numel(), st) == _abi.TP_ERR_WORKSPACE
