@@ -71,7 +71,7 @@ TRAFFIC_RATIO = 1.025
 # DRAM bytes (read 185.44 MB + write 4.13 MB) of one step_kernel launch over
 # the first 4 layers of the Qwen3-4B 3-bit batch-1 line / its algorithmic
 # bytes (169.12 MB); the traffic of every layer is the same, so the ratio
-# scales to the full step (profiles/step_kernel_qwen3-4b_4layer_3bit_b1.md)
+# scales to the full step (ncu --set full on step_kernel, 4-layer bench case)
 STEP_TRAFFIC = {("qwen3-4b", 3, 1): (185_441_024 + 4_134_912) / 169_115_520}
 
 
